@@ -1,0 +1,393 @@
+"""Benchmark of the hybrid-attention hot path.
+
+Workload ("step"): batched hybrid decode -- 64 sequences per GPU, each with a
+ragged KV cache of L_i ~ U{512..32768} cached positions (seeded), advance one
+token through one gated GQA layer (dz_gqa_decode) and one Gated DeltaNet layer
+(dz_gdn_decode).  Inputs are synthetic N(0,1) activations (projections are out
+of scope), KV contents N(0,1), DeltaNet state N(0, 0.02).  Sequence-sharded
+across GPUs with no collective: every rank owns its own 64 sequences (weak
+scaling).  The per-step KV + state traffic (~9 GB) is far above the 126 MB L2,
+so no flush is needed between steps.
+
+Metric: decode tokens/s (whole job), with the achieved HBM GB/s of the
+dominant kernel group against the measured copy bandwidth.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "hybrid-attn decode tok/s + % HBM BW; prefill attn TFLOP/s vs peak"
+B_PER_RANK = 64
+LEN_LO, LEN_HI = 512, 32768
+SEED0 = 0xDA12A000 + 2      # config 2
+
+HQ, HKV, GRP, HD = 24, 4, 6, 256
+SSM_HV, SSM_D, QKV_LEN, INNER = 48, 128, 10240, 6144
+
+
+def seq_lengths(rank):
+    rng = np.random.default_rng(SEED0 + 7919 * rank)
+    return rng.integers(LEN_LO, LEN_HI + 1, size=B_PER_RANK).astype(np.int64)
+
+
+def layer_params(seed):
+    """Seeded synthetic parameters: norm weights ~ U(0.5,1.5), conv w ~ N(0,0.5),
+    ssm_a = -exp(U(0,2.7)), dt_bias = 0."""
+    rng = np.random.default_rng(seed)
+    f = np.float32
+    q_norm = rng.uniform(0.5, 1.5, HD).astype(f)
+    k_norm = rng.uniform(0.5, 1.5, HD).astype(f)
+    conv_w = rng.normal(0.0, 0.5, (4, QKV_LEN)).astype(f)
+    ssm_a = (-np.exp(rng.uniform(0.0, 2.7, SSM_HV))).astype(f)
+    dt_bias = np.zeros(SSM_HV, f)
+    norm_w = rng.uniform(0.5, 1.5, SSM_D).astype(f)
+    return (q_norm, k_norm), (conv_w, ssm_a, dt_bias, norm_w)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# algorithmic bytes (SURVEY 8d formulas, counted per step)
+def gqa_bytes(lens_before):
+    n = np.asarray(lens_before, np.int64) + 1
+    kv_read = int(n.sum()) * HKV * HD * 4 * 2
+    per_seq = HQ * 2 * HD * 4 + HKV * HD * 4 * 2 + HQ * HD * 4      # q_gate in, k/v append, out
+    return kv_read + len(n) * per_seq + 2 * HD * 4
+
+
+def gdn_bytes(B):
+    per_seq = (2 * SSM_HV * SSM_D * SSM_D * 4            # state read + write
+               + 3 * QKV_LEN * 4 + QKV_LEN * 4          # 3 history rows read, 1 written
+               + QKV_LEN * 4 + 2 * SSM_HV * 4           # qkv, alpha, beta
+               + INNER * 4 * 2)                         # z in, y out
+    return B * per_seq + 4 * QKV_LEN * 4 + (2 * SSM_HV + SSM_D) * 4   # + conv weights and params once
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline: the oracle (C++ restatement of the AVX2 path)
+# ---------------------------------------------------------------------------
+class CpuWorkload:
+    """A bounded sample of config 2 for the oracle (C++ restatement of the
+    reference's AVX2 path): n_seq of the 64 sequences (evenly spaced, their real
+    lengths), built once; step() advances every sampled sequence by one token
+    through both layers."""
+
+    def __init__(self, n_seq, max_steps, rank=0):
+        import oracle as O
+        self.O = O
+        lens = seq_lengths(rank)
+        self.pick = lens[:: max(1, B_PER_RANK // n_seq)][:n_seq]
+        (self.qn, self.kn), self.p = layer_params(SEED0)
+        self.kvs, self.sts = [], []
+        for i, n in enumerate(self.pick):
+            kv = O.OracleKv(int(n) + max_steps)
+            kv.k[:, :n] = O.normal(SEED0 + 500 + i, (HKV, int(n), HD))
+            kv.v[:, :n] = O.normal(SEED0 + 600 + i, (HKV, int(n), HD))
+            kv.len = int(n)
+            self.kvs.append(kv)
+            self.sts.append(O.OracleSsm(O.normal(SEED0 + 700 + i, (SSM_HV, SSM_D, SSM_D), 0.0, 0.02),
+                                        O.normal(SEED0 + 800 + i, (4, QKV_LEN)), 0))
+        Bs = len(self.pick)
+        self.qg = O.normal(SEED0 + 1, (Bs, HQ * 2 * HD))
+        self.k = O.normal(SEED0 + 2, (Bs, HKV * HD))
+        self.v = O.normal(SEED0 + 3, (Bs, HKV * HD))
+        self.qkv = O.normal(SEED0 + 4, (Bs, QKV_LEN))
+        self.a = O.normal(SEED0 + 5, (Bs, SSM_HV))
+        self.b = O.normal(SEED0 + 6, (Bs, SSM_HV))
+        self.z = O.normal(SEED0 + 7, (Bs, INNER))
+
+    def step(self, n_threads):
+        t0 = time.perf_counter()
+        self.O.gqa_decode_batch(self.qg, self.k, self.v, self.qn, self.kn, self.kvs, n_threads=n_threads)
+        self.O.gdn_decode_batch(self.qkv, self.a, self.b, self.z, self.p, self.sts, n_threads=n_threads)
+        return time.perf_counter() - t0
+
+
+def cpu_baseline(n_seq_sample=8, steps=1, n_threads=1, rank=0):
+    w = CpuWorkload(n_seq_sample, steps, rank)
+    dt = sum(w.step(n_threads) for _ in range(steps))
+    return len(w.pick) * steps / dt, dt, w.pick
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cores = os.cpu_count() or 1
+    n_seq = min(cores, 32)
+    w = CpuWorkload(n_seq, args.warmup + args.steps, rank)
+    for _ in range(args.warmup):
+        w.step(cores)
+    dts = [w.step(cores) for _ in range(args.steps)]
+    wall = sum(dts)
+    value = len(w.pick) * args.steps / wall
+    sample = (f"{len(w.pick)} of the 64 config-2 sequences (evenly spaced, real lengths, "
+              f"{int(np.sum(w.pick))} cached tokens), one decode step of both layers per timed step; "
+              f"one sequence per thread on {cores} host threads (harness parallelisation: the reference "
+              "decodes one sequence at a time)")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * wall / max(1, args.steps),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "config 2: batched hybrid decode, 64 seqs/GPU, "
+                                                        "KV U{512..32768}, 1 GQA + 1 GDN layer"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import daiza_b200 as dz
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+
+    lens = seq_lengths(rank)
+    total_steps = args.warmup + args.steps + 2
+    cfg = dz.default_config(n_layers=2, full_attention_interval=2)   # layer 0 GDN, layer 1 GQA
+    ctx = dz.Context(local, cfg)
+    (qn, kn), sp = layer_params(SEED0)
+    ctx.set_attn_params(1, qn, kn)
+    ctx.set_ssm_params(0, *sp)
+    ctx.cache_create(lens + total_steps)
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED0 + rank)
+    for s, n in enumerate(lens):
+        kf = torch.randn(int(n), HKV, HD, device=dev, generator=g)
+        vf = torch.randn(int(n), HKV, HD, device=dev, generator=g)
+        ctx.kv_import(1, s, kf, vf)
+        del kf, vf
+        st = torch.randn(SSM_HV, SSM_D, SSM_D, device=dev, generator=g) * 0.02
+        hist = torch.randn(4, QKV_LEN, device=dev, generator=g)
+        ctx.ssm_import(0, s, st, hist, 0)
+    torch.cuda.synchronize()
+    B = B_PER_RANK
+    ids = np.arange(B, dtype=np.int32)
+    qg = torch.randn(B, HQ * 2 * HD, device=dev, generator=g)
+    kk = torch.randn(B, HKV * HD, device=dev, generator=g)
+    vv = torch.randn(B, HKV * HD, device=dev, generator=g)
+    qkv = torch.randn(B, QKV_LEN, device=dev, generator=g)
+    al = torch.randn(B, SSM_HV, device=dev, generator=g)
+    be = torch.randn(B, SSM_HV, device=dev, generator=g)
+    z = torch.randn(B, INNER, device=dev, generator=g)
+    out = torch.empty(B, HQ * HD, device=dev)
+    y = torch.empty(B, INNER, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ctx.gqa_decode(1, ids, qg, kk, vv, out)
+        n1 = ctx.last_launch_count
+        ctx.gdn_decode(0, ids, qkv, al, be, z, y)
+        return n1 + ctx.last_launch_count
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    lens_at = np.array([ctx.kv_len(1, s) for s in range(B)], np.int64)
+    clocks = Clocks(local)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    launches = 0
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        ctx.gqa_decode(1, ids, qg, kk, vv, out)
+        launches += ctx.last_launch_count
+        ev[i][1].record(stream)
+        ctx.gdn_decode(0, ids, qkv, al, be, z, y)
+        launches += ctx.last_launch_count
+        ev[i][2].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t_start.elapsed_time(t_end)
+    gqa_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.steps)]
+    gdn_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps)]
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * B * args.steps / (ms / 1000.0)
+
+    # bytes per step of the dominant kernel group (GQA decode: prep + split-K + combine)
+    gqa_b = np.mean([gqa_bytes(lens_at + i) for i in range(args.steps)])
+    gdn_b = gdn_bytes(B)
+    hbm, bf16, peak_kind = peaks()
+    gqa_gbs = gqa_b / (np.mean(gqa_ms) / 1000.0) / 1e9
+    gdn_gbs = gdn_b / (np.mean(gdn_ms) / 1000.0) / 1e9
+    step_gbs = (gqa_b + gdn_b) / (ms / args.steps / 1000.0) / 1e9
+
+    # end-to-end through the public C ABI host entry points (pinned host buffers)
+    e2e = None
+    if args.e2e_steps > 0:
+        hq = torch.empty(B, HQ * 2 * HD, pin_memory=True)
+        hq.copy_(qg.cpu())
+        hk = kk.cpu().pin_memory()
+        hv = vv.cpu().pin_memory()
+        hx = qkv.cpu().pin_memory()
+        ha = al.cpu().pin_memory()
+        hb = be.cpu().pin_memory()
+        hz = z.cpu().pin_memory()
+        ho = torch.empty(B, HQ * HD, pin_memory=True)
+        hy = torch.empty(B, INNER, pin_memory=True)
+        np_views = [t.numpy() for t in (hq, hk, hv, hx, ha, hb, hz, ho, hy)]
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            ctx.gqa_decode_host(1, ids, np_views[0], np_views[1], np_views[2], np_views[7])
+            ctx.gdn_decode_host(0, ids, np_views[3], np_views[4], np_views[5], np_views[6], np_views[8])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        h2d = B * (HQ * 2 * HD + 2 * HKV * HD + QKV_LEN + 2 * SSM_HV + INNER) * 4
+        d2h = B * (HQ * HD + INNER) * 4
+        e2e = {"value": world * B * args.e2e_steps / (ems / 1000.0), "unit": "tok/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "dz_gqa_decode_host + dz_gdn_decode_host (pinned host buffers, copies inside the timed region)",
+               "steps": args.e2e_steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, dt, pick = cpu_baseline(n_seq_sample=8, steps=args.cpu_steps, n_threads=1)
+        cpu = {"value": v, "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": f"8 of the 64 sequences (lengths {list(map(int, pick))}), {args.cpu_steps} decode step(s) "
+                         f"of both layers, single thread like the reference's decode attention/scan; {dt:.2f} s"}
+
+    err = ctx.device_error()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "config 2: batched hybrid decode, 64 seqs/GPU, KV lengths U{512..32768} "
+                                       "(seeded), 1 gated GQA + 1 Gated DeltaNet layer, f32 caches",
+                           "seqs_per_gpu": B, "kv_tokens_per_gpu": int(lens_at.sum()),
+                           "parallelism": f"sequence-sharded x{world}, no collective",
+                           "l2": "no flush: per-step KV+state traffic ~9 GB >> 126 MB L2"},
+                "hbm_gbs_step": step_gbs, "hbm_frac_step": step_gbs / hbm,
+                "roofline": {"bound": "hbm", "kernel": "dz_gqa_decode (prep + split-K + combine)",
+                             "achieved": gqa_gbs, "peak": hbm, "unit": "GB/s", "frac": gqa_gbs / hbm,
+                             "traffic": None, "peak_kind": f"{peak_kind} hbm_gbs",
+                             "bytes_per_launch": gqa_b, "ms_per_launch": float(np.mean(gqa_ms))},
+                "gdn": {"achieved_gbs": gdn_gbs, "frac": gdn_gbs / hbm, "bytes": gdn_b,
+                        "ms": float(np.mean(gdn_ms))},
+                "gpu_launches": launches, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
+                "device_error": err}
+        print(json.dumps(line))
+    ctx.close()
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-steps", type=int, default=1)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,98 @@
+// dz_internal.h -- host-side context and launcher declarations for libdzattn.
+#pragma once
+#include <string>
+#include <vector>
+#include <cuda_runtime.h>
+
+#include "../../include/dz_attn.h"
+#include "dz_common.cuh"
+
+namespace dz {
+
+constexpr int MAXB = 256;   // sequences per kernel launch (descriptor rides in the kernel parameters)
+constexpr int MAXC = 128;   // max split-K chunks per (sequence, kv head) in decode
+
+// One sequence's KV cache for one full-attention layer:
+//   k, v: [kv_head_count][cap][256] f32 -- per kv head a contiguous [seq, dim]
+//   block, the reference's layout (Daiza-engine/src/cache/kv_cache.rs:16-28).
+struct KvSlot { float* k; float* v; int64_t cap; };
+// One sequence's SsmState for one Gated DeltaNet layer (cache/ssm_state.rs:9-21):
+//   state [v_head_count][128][128] f32 (row = v index, col = k index),
+//   hist  [4][10240] f32 conv ring (slot `head` is the oldest row).
+struct SsmSlot { float* state; float* hist; };
+
+// Per-launch batch descriptor for GQA decode (passed by value as a kernel parameter).
+struct GqaDecodeDesc {
+    int B;
+    int chunk;                 // positions per split-K chunk (multiple of 16)
+    int32_t sid[MAXB];         // sequence slot of batch row b
+    int32_t len[MAXB];         // cache length before this token = slot = RoPE position
+    int32_t cum[MAXB + 1];     // prefix sum of chunks(b) = ceil((len+1)/chunk)
+};
+
+struct GdnDecodeDesc {
+    int B;
+    int32_t sid[MAXB];
+    int32_t head[MAXB];        // conv ring head before this token
+};
+
+struct LayerState {
+    bool is_attn = false;
+    bool params_set = false;
+    float* q_norm = nullptr;   // [256]
+    float* k_norm = nullptr;   // [256]
+    float* conv_w = nullptr;   // [4][10240]
+    float* ssm_a = nullptr;    // [48]
+    float* dt_bias = nullptr;  // [48]
+    float* norm_w = nullptr;   // [128]
+    KvSlot* d_kv = nullptr;    // [n_seqs]
+    std::vector<KvSlot> h_kv;
+    std::vector<int64_t> len;  // host-authoritative KvCache::len
+    SsmSlot* d_ssm = nullptr;  // [n_seqs]
+    std::vector<SsmSlot> h_ssm;
+    std::vector<int32_t> head; // host-authoritative SsmState::conv_head
+};
+
+}  // namespace dz
+
+struct dz_ctx {
+    int device = 0;
+    int n_sm = 148;
+    dz_config cfg{};
+    std::string err;
+    int last_launches = 0;
+    std::vector<dz::LayerState> layers;
+    int n_seqs = 0;
+    std::vector<int64_t> caps;
+    float* rope = nullptr;      // [rope_n][128] = cos[64] | sin[64]
+    int64_t rope_n = 0;
+    std::vector<void*> cache_allocs;
+    // decode scratch (owned by the context, sized at dz_cache_create)
+    float* q_buf = nullptr;     // [n_seqs][6*kvc][256]
+    float* part_o = nullptr;    // [items][6][256] unnormalised split-K outputs
+    float* part_ml = nullptr;   // [items][6][2]  (running max in log2 units, sum)
+    int64_t part_items = 0;
+    int* d_err = nullptr;       // device error word
+    // staging for the *_host entry points (grown on demand)
+    void* stage = nullptr;
+    size_t stage_bytes = 0;
+    // prefill scratch (grown on demand)
+    void* pf = nullptr;
+    size_t pf_bytes = 0;
+};
+
+namespace dz {
+// launchers (return cudaError_t of the last launch)
+cudaError_t launch_gqa_decode(dz_ctx* ctx, int layer, const GqaDecodeDesc& d, const float* q_gate,
+                              const float* k, const float* v, float* out, cudaStream_t st, int* n_launch);
+cudaError_t launch_gdn_decode(dz_ctx* ctx, int layer, const GdnDecodeDesc& d, const float* qkv,
+                              const float* alpha, const float* beta, const float* z, float* y,
+                              cudaStream_t st, int* n_launch);
+cudaError_t launch_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const uint16_t* q_gate,
+                               const uint16_t* k, const uint16_t* v, const float* q_gate_f, const float* k_f,
+                               const float* v_f, float* out, cudaStream_t st, int* n_launch);
+cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* qkv, const float* alpha,
+                               const float* beta, const float* z, float* y, cudaStream_t st, int* n_launch);
+// grows ctx->pf to at least `bytes`
+cudaError_t ensure_prefill_scratch(dz_ctx* ctx, size_t bytes);
+}  // namespace dz

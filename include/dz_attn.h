@@ -1,0 +1,164 @@
+/* dz_attn.h -- C ABI of the B200-native hybrid-attention core (libdzattn.so).
+ *
+ * This is the drop-in boundary for Daiza's per-layer attention / Gated DeltaNet
+ * core: everything after the Q/K/V (or qkv/alpha/beta/z) projection GEMV and
+ * before the output projection.  Citations are paths inside guang384/Daiza.
+ *
+ * Conventions
+ *  - Every function returns dz_status; DZ_OK == 0.  dz_last_error(ctx) gives a
+ *    human-readable message for the last failure on that context.
+ *  - Compute entry points take DEVICE pointers for tensors and a cudaStream_t
+ *    passed as void*; they are stream-ordered and never synchronise.  Sequence
+ *    ids are HOST int32 arrays: cache lengths and conv-ring heads are kept on
+ *    the host (as KvCache::len and SsmState::conv_head are host fields in the
+ *    reference), so the library sizes every launch without a device round
+ *    trip.  The *_host variants take HOST tensors, stage them through the
+ *    context and block until the output is back.
+ *  - A context is used by one host thread at a time (the reference's model is
+ *    a single owner thread calling forward; model/block.rs:53-81).
+ *  - Shapes are the Bonsai-27B ones (Daiza-engine/src/model/config.rs:47-74):
+ *    24 q heads / 4 kv heads / head_dim 256 / rope_dim 64 for full attention;
+ *    16 k heads / 48 v heads / d 128 / conv 4 for Gated DeltaNet.  A context
+ *    may own a contiguous slice of the heads (head sharding across GPUs).
+ */
+#ifndef DZ_ATTN_H
+#define DZ_ATTN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    DZ_OK = 0,
+    DZ_EINVAL = 1,    /* bad argument / shape / layer kind */
+    DZ_ENOMEM = 2,    /* device or host allocation failed */
+    DZ_ECUDA = 3,     /* a CUDA runtime call failed */
+    DZ_ENCCL = 4,     /* reserved for collective failures */
+    DZ_ETIMEOUT = 5,  /* a bounded wait ran out */
+    DZ_ESTATE = 6     /* call order violated (e.g. no cache yet, cache full) */
+} dz_status;
+
+typedef struct dz_ctx dz_ctx;
+
+/* Model constants; mirrors Config (Daiza-engine/src/model/config.rs:5-45,47-74)
+ * plus the head slice this context owns. */
+typedef struct dz_config {
+    int32_t n_layers;                 /* block_count */
+    int32_t full_attention_interval;  /* layer i is GQA iff i % interval == interval-1 (config.rs:161-166) */
+    int32_t head_count;               /* 24 */
+    int32_t head_count_kv;            /* 4 */
+    int32_t head_dim;                 /* 256 */
+    int32_t rope_dim;                 /* 64 */
+    float   rope_freq_base;           /* 1e7 */
+    float   rms_eps;                  /* 1e-6 */
+    int32_t ssm_conv_kernel;          /* 4 */
+    int32_t ssm_state_size;           /* 128 */
+    int32_t ssm_group_count;          /* 16 k heads */
+    int32_t ssm_time_step_rank;       /* 48 v heads */
+    int32_t ssm_inner_size;           /* 6144 */
+    /* head slice owned by this context (head sharding); defaults: everything */
+    int32_t kv_head_begin, kv_head_count;   /* GQA kv heads [begin, begin+count) */
+    int32_t v_head_begin, v_head_count;     /* GDN v heads  [begin, begin+count) */
+} dz_config;
+
+/* Fills the Bonsai-27B defaults (Config::default, config.rs:47-74). */
+dz_status dz_config_default(dz_config* cfg);
+
+/* Context on one CUDA device.  Replaces the ModelState owner
+ * (Daiza-engine/src/model/forward.rs:32-77) for the attention/SSM caches. */
+dz_status dz_ctx_create(int device, const dz_config* cfg, dz_ctx** out);
+dz_status dz_ctx_destroy(dz_ctx* ctx);
+const char* dz_last_error(const dz_ctx* ctx);
+/* 1 if layer is full attention, 0 if Gated DeltaNet (config.rs:161-166). */
+int dz_layer_is_attention(const dz_ctx* ctx, int layer);
+
+/* ---- layer parameters (host f32 pointers, copied to HBM once) ----------- */
+/* attn_q_norm, attn_k_norm [256]  (FullAttentionBlockWeights, weights.rs:1248-1259) */
+dz_status dz_layer_set_attn_params(dz_ctx* ctx, int layer, const float* q_norm, const float* k_norm);
+/* ssm_conv1d transposed [4][10240] (weights.rs:1339-1356), ssm_a [48] (= -exp(A_log)),
+ * ssm_dt_bias [48], ssm_norm [128]  (SsmBlockWeights, weights.rs:1229-1246) */
+dz_status dz_layer_set_ssm_params(dz_ctx* ctx, int layer, const float* conv1d_t, const float* ssm_a,
+                                  const float* dt_bias, const float* ssm_norm);
+
+/* ---- caches ------------------------------------------------------------- */
+/* Allocates, for n_seqs sequence slots, a KV cache per full-attention layer
+ * with capacity max_len[s] tokens (KvCache::new, cache/kv_cache.rs:34-40) and
+ * an SsmState per Gated DeltaNet layer, zero state, zero conv history, head 0
+ * (SsmState::new, cache/ssm_state.rs:24-32).  Also uploads the RoPE table for
+ * positions [0, max(max_len)) computed with the reference formula
+ * (math/rope.rs:27-38,82-101).  Replaces any previous cache set. */
+dz_status dz_cache_create(dz_ctx* ctx, int n_seqs, const int64_t* max_len);
+/* KvCache::len (kv_cache.rs:23) */
+dz_status dz_kv_len(const dz_ctx* ctx, int layer, int seq, int64_t* out_len);
+/* KvCache::truncate (kv_cache.rs:119-129): no-op if new_len >= len. */
+dz_status dz_kv_truncate(dz_ctx* ctx, int layer, int seq, int64_t new_len);
+/* KvCache::reset + SsmState::reset for every layer of one sequence
+ * (kv_cache.rs:109-115, ssm_state.rs:34-39). */
+dz_status dz_cache_reset(dz_ctx* ctx, int seq);
+/* Export K and V as flat host [len][kv_head_count][256] f32, the DZSS session
+ * layout (Daiza-runtime/src/session_persist.rs:106-118).  Bit-exact placement. */
+dz_status dz_kv_export(dz_ctx* ctx, int layer, int seq, float* k_flat, float* v_flat);
+/* KvCache::from_raw (kv_cache.rs:46-67): flat [len][kv_head_count][256].
+ * Export/import buffers may be host or device pointers (unified addressing). */
+dz_status dz_kv_import(dz_ctx* ctx, int layer, int seq, const float* k_flat, const float* v_flat, int64_t len);
+/* SsmState fields (ssm_state.rs:9-21): state [v_head_count][128][128],
+ * conv_history [4][10240] (only the channels this context uses are kept on
+ * device; the others export as 0), conv_head. Host pointers. */
+dz_status dz_ssm_export(dz_ctx* ctx, int layer, int seq, float* state, float* conv_history, int32_t* conv_head);
+dz_status dz_ssm_import(dz_ctx* ctx, int layer, int seq, const float* state, const float* conv_history,
+                        int32_t conv_head);
+/* The device RoPE table rows [pos0, pos0+n): cos[64] | sin[64] per row (host out). */
+dz_status dz_rope_table(dz_ctx* ctx, int64_t pos0, int64_t n, float* out);
+
+/* ---- compute: decode (one new token per sequence) ----------------------- */
+/* Gated GQA core of attention_forward_into (model/attention.rs:90-203):
+ * deinterleave [Q_h|gate_h], QK-RMSNorm, partial RoPE at pos = len, q *= 1/16,
+ * KV append at slot len, online-softmax attention over len+1 positions,
+ * * sigmoid(gate).  B sequences; seq_ids (host int32 [B], distinct) name the slots.
+ *   q_gate [B][6*kvc][512]  (the [Q_h|gate_h] rows of this context's q heads)
+ *   k, v   [B][kvc][256]     out [B][6*kvc][256]      (kvc = kv_head_count)  */
+dz_status dz_gqa_decode(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* q_gate,
+                        const float* k, const float* v, float* out, void* stream);
+/* Gated DeltaNet core of ssm_forward_into (model/ssm.rs:466-611): ring conv1d
+ * + SiLU, L2-norm q/k, q *= 1/sqrt(128), gates, gated delta rule on the
+ * [v][k] state, gated RMSNorm output.
+ *   qkv [B][10240] (full row; the context reads the channels it needs),
+ *   alpha, beta [B][48], z [B][48*128], y [B][v_head_count*128]          */
+dz_status dz_gdn_decode(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* qkv,
+                        const float* alpha, const float* beta, const float* z, float* y, void* stream);
+
+/* ---- compute: prefill (T tokens of one sequence) ------------------------ */
+/* Parallel GQA prefill (model/forward.rs:599-721), positions len..len+T-1.
+ * q_gate/k/v are bf16 (uint16 bit patterns) rows as above; out f32 [T][6*kvc][256].
+ * Attention products run on the tensor cores in bf16 with f32 accumulation. */
+dz_status dz_gqa_prefill_bf16(dz_ctx* ctx, int layer, int seq, int64_t T, const uint16_t* q_gate,
+                              const uint16_t* k, const uint16_t* v, float* out, void* stream);
+/* Same with f32 inputs (converted on device). */
+dz_status dz_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* q_gate, const float* k,
+                         const float* v, float* out, void* stream);
+/* Chunked (C=64) Gated DeltaNet prefill equal to the token-recurrent reference
+ * (model/forward.rs:897-1059).  qkv [T][10240], alpha/beta [T][48], z [T][6144],
+ * y [T][v_head_count*128]. */
+dz_status dz_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* qkv, const float* alpha,
+                         const float* beta, const float* z, float* y, void* stream);
+
+/* ---- host-buffer convenience (end-to-end path) -------------------------- */
+/* Same as dz_gqa_decode / dz_gdn_decode with HOST input/output pointers and
+ * HOST seq_ids; copies in, computes, copies out on `stream`, then waits. */
+dz_status dz_gqa_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* q_gate,
+                             const float* k, const float* v, float* out, void* stream);
+dz_status dz_gdn_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* qkv,
+                             const float* alpha, const float* beta, const float* z, float* y, void* stream);
+
+/* Number of kernels launched by the last compute call on this context. */
+int dz_last_launch_count(const dz_ctx* ctx);
+/* Synchronises the context's device and reads (then clears) the device error
+ * word that kernels set when a bounded wait runs out; *code = 0 if none. */
+dz_status dz_device_error(dz_ctx* ctx, int32_t* code);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DZ_ATTN_H */
