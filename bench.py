@@ -85,13 +85,14 @@ class Clocks:
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device):
-        self.device = device
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id          # nvidia-smi id (UUID), independent of CUDA_VISIBLE_DEVICES
         self.proc = None
+        self.raw = ""
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
@@ -106,6 +107,7 @@ class Clocks:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
+        self.raw = out
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.strip().splitlines():
@@ -217,8 +219,8 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
 
-    lens = seq_lengths(rank)
-    total_steps = args.warmup + args.steps + 2
+    lens = seq_lengths(rank)[: args.seqs]
+    total_steps = args.warmup + args.steps + args.e2e_steps + 2
     cfg = dz.default_config(n_layers=2, full_attention_interval=2)   # layer 0 GDN, layer 1 GQA
     ctx = dz.Context(local, cfg)
     (qn, kn), sp = layer_params(SEED0)
@@ -236,7 +238,7 @@ def run_ours(args):
         hist = torch.randn(4, QKV_LEN, device=dev, generator=g)
         ctx.ssm_import(0, s, st, hist, 0)
     torch.cuda.synchronize()
-    B = B_PER_RANK
+    B = len(lens)
     ids = np.arange(B, dtype=np.int32)
     qg = torch.randn(B, HQ * 2 * HD, device=dev, generator=g)
     kk = torch.randn(B, HKV * HD, device=dev, generator=g)
@@ -263,7 +265,8 @@ def run_ours(args):
     torch.cuda.synchronize()
 
     lens_at = np.array([ctx.kv_len(1, s) for s in range(B)], np.int64)
-    clocks = Clocks(local)
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    clocks = Clocks(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
     clocks.start()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -365,6 +368,8 @@ def run_ours(args):
                         "ms": float(np.mean(gdn_ms))},
                 "gpu_launches": launches, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
                 "device_error": err}
+        if clk is None and clocks.raw:
+            line["clocks_raw_head"] = clocks.raw[:300]
         print(json.dumps(line))
     ctx.close()
     if dist:
@@ -381,6 +386,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-steps", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--seqs", type=int, default=B_PER_RANK,
+                    help="sequences per GPU (default 64 = config 2; smaller only for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
