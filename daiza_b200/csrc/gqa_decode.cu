@@ -315,3 +315,23 @@ cudaError_t launch_gqa_decode(dz_ctx* ctx, int layer, const GqaDecodeDesc& d, co
 }
 
 }  // namespace dz
+
+namespace dz {
+// Same three launches as launch_gqa_decode, with the split-K scratch supplied by
+// the caller instead of taken from the context (used by the no-allocation entry
+// point, whose scratch is a fixed device array).
+cudaError_t launch_gqa_decode_scratch(dz_ctx* ctx, int layer, const GqaDecodeDesc& d, const float* q_gate,
+                                      const float* k, const float* v, float* out, cudaStream_t st, int* n_launch,
+                                      float* q_buf, float* part_o, float* part_ml) {
+    const LayerState& L = ctx->layers[layer];
+    const int kvc = ctx->cfg.kv_head_count;
+    const int items = d.cum[d.B] * kvc;
+    cudaFuncSetAttribute(gqa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SplitSmem));
+    gqa_prep_kernel<<<d.B, 256, 0, st>>>(d, kvc, L.d_kv, L.q_norm, L.k_norm, ctx->rope, q_gate, k, v, q_buf,
+                                         ctx->cfg.rms_eps);
+    gqa_split_kernel<<<items, 128, sizeof(SplitSmem), st>>>(d, kvc, L.d_kv, q_buf, part_o, part_ml, ctx->d_err);
+    gqa_combine_kernel<<<dim3(kvc, d.B), 256, 0, st>>>(d, kvc, part_o, part_ml, q_gate, out);
+    *n_launch += 3;
+    return cudaGetLastError();
+}
+}  // namespace dz

@@ -152,6 +152,22 @@ dz_status dz_gqa_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_i
 dz_status dz_gdn_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* qkv,
                              const float* alpha, const float* beta, const float* z, float* y, void* stream);
 
+/* dz_gqa_decode without any device allocation, for callers that cannot call
+ * cudaMalloc: engines whose device memory is owned end to end by their own
+ * allocator, and decode loops that must not risk the implicit device
+ * synchronisation of cudaMalloc/cudaFree.  Same arguments, semantics and cache
+ * updates as dz_gqa_decode; its split-K scratch lives in one fixed device array
+ * inside the library (about 13.6 MiB per GPU that loads the library, held until
+ * exit).  Limits: at most 64 sequences per call (DZ_EINVAL beyond that); the
+ * split-K chunk grows so that a call needs at most 2048 work items.  All calls
+ * on a device share the array: calls that overlap on the GPU race, so order
+ * them.  The first call on each device looks up the array's device address;
+ * make that first call before any stream capture begins.
+ * No counterpart in the reference (the reference runs on the CPU and never
+ * allocates device memory). */
+dz_status dz_gqa_decode_noalloc(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* q_gate,
+                                const float* k, const float* v, float* out, void* stream);
+
 /* Number of kernels launched by the last compute call on this context. */
 int dz_last_launch_count(const dz_ctx* ctx);
 /* Synchronises the context's device and reads (then clears) the device error
