@@ -490,17 +490,17 @@ static dz_status gqa_decode_impl(dz_ctx* ctx, int layer, int B, const int32_t* s
         const int nb = std::min(MAXB, B - b0);
         GqaDecodeDesc d;
         d.B = nb;
-        // split-K chunk: aim for ~4 CTAs per SM over the whole batch, 32..1024 positions,
-        // at most MAXC chunks per (sequence, kv head)
+        // split-K chunk (positions per warp work item): ~4 items per resident warp
+        // (4 warps per SM) over the whole batch, 16..1024 positions, at most MAXC
+        // chunks per (sequence, kv head)
         int64_t total = 0, nmax = 0;
         for (int b = 0; b < nb; ++b) {
             const int64_t n = L.len[seq_ids[b0 + b]] + 1;
             total += n;
             nmax = std::max(nmax, n);
         }
-        int64_t chunk = (total * kvc) / ((int64_t)ctx->n_sm * 4);
-        chunk = std::max<int64_t>(chunk, (nmax + MAXC - 1) / MAXC);
-        chunk = std::min<int64_t>(std::max<int64_t>(chunk, 32), 1024);
+        int64_t chunk = (total * kvc) / ((int64_t)ctx->n_sm * 16);
+        chunk = std::min<int64_t>(std::max<int64_t>(chunk, 16), 1024);
         chunk = std::max<int64_t>(chunk, (nmax + MAXC - 1) / MAXC);
         chunk = (chunk + 15) / 16 * 16;
         d.chunk = (int)chunk;

@@ -13,6 +13,8 @@
 //     back with one 16 KB bulk store;
 //   - the gated RMSNorm output y * inv_rms * w * silu(z) (ssm.rs:576-611).
 // State traffic is exactly one read and one write of each tile.
+#include <cstddef>
+
 #include "dz_internal.h"
 
 namespace dz {
@@ -24,6 +26,7 @@ struct GdnSmem {
     float gate[2];           // decay, beta
     uint64_t bar[4];
 };
+static_assert(offsetof(GdnSmem, q) % 16 == 0 && offsetof(GdnSmem, k) % 16 == 0, "float4-read fields aligned");
 
 __device__ __forceinline__ float block_sum128(float x, float* red4) {
     x = warp_sum(x);

@@ -5,22 +5,24 @@
 //   1. gqa_prep     : per sequence -- deinterleave [Q_h|gate_h], QK-RMSNorm,
 //                     partial RoPE (the reference's '+' sign, math/rope.rs:205-210)
 //                     at pos = len, q *= 1/16, append K/V at slot len.
-//   2. gqa_split    : per (sequence, split-K chunk, kv head) -- the 6 grouped q
-//                     heads attend over the chunk's cached positions.  K/V tiles
-//                     of 16 positions stream HBM -> shared memory through 1-D
-//                     bulk async copies (cp.async.bulk + mbarrier, 3 stages);
-//                     scores on the FP32 pipes, online softmax in log2 units
-//                     with warp-shuffle reductions, unnormalised partials out.
+//   2. gqa_split    : per (sequence, split-K chunk, kv head), one warp each --
+//                     the 6 grouped q heads attend over the chunk's cached
+//                     positions.  K/V tiles of 8 positions stream HBM -> shared
+//                     memory through 1-D bulk async copies (cp.async.bulk +
+//                     mbarrier, 3 stages per warp); scores on the FP32 pipes
+//                     with a warp-shuffle reduce-scatter, online softmax in
+//                     log2 units, unnormalised partials out.
 //   3. gqa_combine  : per (sequence, kv head) -- merge the chunks' (m, l, o),
 //                     divide, multiply by sigmoid(gate).
 // Memory bound: every cached K and V byte is read exactly once.
+#include <algorithm>
+#include <cstddef>
+
 #include "dz_internal.h"
 
 namespace dz {
 
-constexpr int TILE = 16;      // positions per pipeline stage
 constexpr int STAGES = 3;
-constexpr int KPAD = 260;     // padded K row in shared memory (floats): conflict-free row-per-lane reads
 
 // ---------------------------------------------------------------------------
 // 1. prep: 8 warps, one head task per warp-iteration.  tasks [0, nq) are q heads,
@@ -96,169 +98,239 @@ __global__ void __launch_bounds__(256) gqa_prep_kernel(GqaDecodeDesc d, int kvc,
 }
 
 // ---------------------------------------------------------------------------
-// 2. split-K attention over one chunk
+// 2. split-K attention, one WARP per work item (sequence, chunk, kv head).
+//    Persistent CTAs of 4 independent warps (one CTA per SM).  Each warp walks
+//    its own items and keeps its own ring of STAGES tiles of 8 positions in
+//    shared memory, refilled by its lane 0 with two 1-D bulk async copies per
+//    tile (K rows and V rows are each one contiguous run), across item
+//    boundaries.  No CTA-wide barrier after set-up.
+//    Lane l owns dims [4l,4l+4) and [128+4l,128+4l+4) of q (6 heads, in
+//    registers), K, V and the output accumulators.
+//    QK: 48 partial dot products per lane (8 positions x 6 heads), combined by
+//        a 5-level reduce-scatter (48 shuffles per tile).
+//    softmax: lanes 0..5 own heads (running max in log2 units, sum).
+//    PV: every lane accumulates its 8 dims x 6 heads.
 // ---------------------------------------------------------------------------
-struct SplitSmem {
-    float q[GRP][HD];                 // 6 KB
-    float k[STAGES][TILE][KPAD];      // padded rows
-    float v[STAGES][TILE][HD];
-    float red[4][TILE][8];            // per-warp partial scores [warp][pos][head]
-    float p[TILE][8];                 // probabilities [pos][head]
-    float m[8], l[8], alpha[8];
+constexpr int TP = 8;        // positions per tile
+constexpr int NWARP = 4;     // warps per CTA
+
+// alignas(128): every warp's ring (and its K/V tiles, the bulk-copy
+// destinations) must start on a 16-byte boundary, so the struct size must be a
+// multiple of 16 -- the trailing mbarriers alone would only give 8.
+struct alignas(128) WarpRing {
+    float k[STAGES][TP][HD];
+    float v[STAGES][TP][HD];
+    float sc[TP][8];          // scores [pos][head] (log2 units)
+    float p[TP][8];           // probabilities [pos][head]
+    float alpha[8];
     uint64_t full[STAGES];
 };
+struct SplitSmem {
+    WarpRing w[NWARP];
+};
+static_assert(sizeof(WarpRing) % 128 == 0, "per-warp rings must stay 16-byte aligned");
+static_assert(offsetof(WarpRing, v) % 16 == 0 && offsetof(WarpRing, p) % 16 == 0 &&
+              offsetof(WarpRing, alpha) % 16 == 0, "vector-loaded fields must be 16-byte aligned");
 
-__device__ __forceinline__ void issue_tile(SplitSmem& sm, int stage, int rows, const float* kb, const float* vb,
-                                           int lane) {
-    if (lane == 0) mbar_arrive_expect_tx(&sm.full[stage], (uint32_t)rows * HD * 4 * 2);
-    __syncwarp();
-    if (lane < rows) bulk_g2s(&sm.k[stage][lane][0], kb + (size_t)lane * HD, HD * 4, &sm.full[stage]);
-    if (lane == 31) bulk_g2s(&sm.v[stage][0][0], vb, (uint32_t)rows * HD * 4, &sm.full[stage]);
-}
+struct ItemInfo {
+    int b, kvh, p0, p1, ntiles;
+    const float* kb;
+    const float* vb;
+};
 
-__global__ void __launch_bounds__(128, 2) gqa_split_kernel(GqaDecodeDesc d, int kvc, const KvSlot* __restrict__ kv,
-                                                           const float* __restrict__ q_buf,
-                                                           float* __restrict__ part_o,
-                                                           float* __restrict__ part_ml, int* err) {
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    SplitSmem& sm = *reinterpret_cast<SplitSmem*>(smem_raw);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int item = blockIdx.x;
+__device__ __forceinline__ ItemInfo decode_item(const GqaDecodeDesc& d, int kvc, const KvSlot* __restrict__ kv,
+                                                int item) {
+    ItemInfo it;
     const int chunk_idx = item / kvc;
-    const int kvh = item - chunk_idx * kvc;
-    // b = last index with cum[b] <= chunk_idx
-    int lo = 0, hi = d.B - 1;
+    it.kvh = item - chunk_idx * kvc;
+    int lo = 0, hi = d.B - 1;                    // last b with cum[b] <= chunk_idx
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
         if (d.cum[mid] <= chunk_idx) lo = mid; else hi = mid - 1;
     }
-    const int b = lo;
-    const int c = chunk_idx - d.cum[b];
-    const int n = d.len[b] + 1;
-    const int p0 = c * d.chunk;
-    const int p1 = min(n, p0 + d.chunk);
-    const int ntiles = (p1 - p0 + TILE - 1) / TILE;
-    const KvSlot slot = kv[d.sid[b]];
-    const float* kbase = slot.k + ((size_t)kvh * slot.cap + p0) * HD;
-    const float* vbase = slot.v + ((size_t)kvh * slot.cap + p0) * HD;
+    it.b = lo;
+    const int c = chunk_idx - d.cum[lo];
+    const int n = d.len[lo] + 1;
+    it.p0 = c * d.chunk;
+    it.p1 = min(n, it.p0 + d.chunk);
+    it.ntiles = (it.p1 - it.p0 + TP - 1) / TP;
+    const KvSlot slot = kv[d.sid[lo]];
+    it.kb = slot.k + ((size_t)it.kvh * slot.cap + it.p0) * HD;
+    it.vb = slot.v + ((size_t)it.kvh * slot.cap + it.p0) * HD;
+    return it;
+}
 
-    if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) mbar_init(&sm.full[s], 1);
+// keep the half of `in` selected by `hi` and add the partner lane's other half
+template <int N>
+__device__ __forceinline__ void rs_level(const float (&in)[2 * N], float (&out)[N], bool hi, int mask) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const float send = hi ? in[i] : in[N + i];
+        const float keep = hi ? in[N + i] : in[i];
+        out[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+    }
+}
+
+__global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaDecodeDesc d, int kvc, const KvSlot* __restrict__ kv,
+                                                           const float* __restrict__ q_buf,
+                                                           float* __restrict__ part_o,
+                                                           float* __restrict__ part_ml, int* err, int n_items) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    SplitSmem& smem = *reinterpret_cast<SplitSmem*>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    WarpRing& R = smem.w[warp];
+    const int gw = blockIdx.x * NWARP + warp;
+    const int nw = gridDim.x * NWARP;
+
+    if (lane == 0) {
+        for (int s = 0; s < STAGES; ++s) mbar_init(&R.full[s], 1);
         fence_mbar_init();
     }
-    if (tid < 8) { sm.m[tid] = -INFINITY; sm.l[tid] = 0.0f; sm.alpha[tid] = 1.0f; }
-    {
-        const float4* qs = reinterpret_cast<const float4*>(q_buf + ((size_t)b * GRP * kvc + (size_t)kvh * GRP) * HD);
-        float4* qd = reinterpret_cast<float4*>(&sm.q[0][0]);
-        for (int i = tid; i < GRP * HD / 4; i += 128) qd[i] = qs[i];
-    }
-    __syncthreads();
-    if (warp == 0) {
-        for (int j = 0; j < STAGES && j < ntiles; ++j) {
-            const int rows = min(TILE, p1 - (p0 + j * TILE));
-            issue_tile(sm, j, rows, kbase + (size_t)j * TILE * HD, vbase + (size_t)j * TILE * HD, lane);
-        }
-    }
+    __syncwarp();
 
-    // thread roles
-    const int qp = tid & 15;          // QK: position within tile
-    const int qg = tid >> 4;          // QK: dim group of 32
-    float o[GRP][2];
-#pragma unroll
-    for (int h = 0; h < GRP; ++h) { o[h][0] = 0.0f; o[h][1] = 0.0f; }
-    bool ok = true;
+    // producer cursor (lane 0 issues, all lanes track it uniformly)
+    int p_item = gw, p_tile = 0;
+    ItemInfo pinfo{};
+    if (p_item < n_items) pinfo = decode_item(d, kvc, kv, p_item);
+    auto produce = [&](int stage) {
+        if (p_item >= n_items) return;
+        const int rows = min(TP, pinfo.p1 - (pinfo.p0 + p_tile * TP));
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&R.full[stage], (uint32_t)rows * HD * 4 * 2);
+            bulk_g2s(&R.k[stage][0][0], pinfo.kb + (size_t)p_tile * TP * HD, (uint32_t)rows * HD * 4, &R.full[stage]);
+            bulk_g2s(&R.v[stage][0][0], pinfo.vb + (size_t)p_tile * TP * HD, (uint32_t)rows * HD * 4, &R.full[stage]);
+        }
+        if (++p_tile == pinfo.ntiles) {
+            p_item += nw;
+            p_tile = 0;
+            if (p_item < n_items) pinfo = decode_item(d, kvc, kv, p_item);
+        }
+    };
+    for (int s = 0; s < STAGES; ++s) produce(s);
 
-    for (int j = 0; j < ntiles; ++j) {
-        const int stage = j % STAGES;
-        const int rows = min(TILE, p1 - (p0 + j * TILE));
-        if (!mbar_wait(&sm.full[stage], (uint32_t)((j / STAGES) & 1), err)) { ok = false; }
-        if (__syncthreads_or(!ok)) { ok = false; break; }
-        // ---- scores: thread (qp, qg) covers 32 dims of one position for 6 heads
+    const int k_grp = lane >> 1;              // reduce-scatter group: indices 3k..3k+2 of (pos*6 + head)
+    const int my_pos = k_grp >> 1;
+    const int my_h0 = 3 * (k_grp & 1);
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+    int j = 0;
+    for (int item = gw; item < n_items; item += nw) {
+        const ItemInfo it = decode_item(d, kvc, kv, item);
+        float4 q[GRP][2];
         {
-            float acc[GRP];
-#pragma unroll
-            for (int h = 0; h < GRP; ++h) acc[h] = 0.0f;
-            const float* krow = &sm.k[stage][qp][qg * 32];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float4 kk = *reinterpret_cast<const float4*>(krow + 4 * i);
-#pragma unroll
-                for (int h = 0; h < GRP; ++h) {
-                    const float4 qq = *reinterpret_cast<const float4*>(&sm.q[h][qg * 32 + 4 * i]);
-                    acc[h] = fmaf(kk.x, qq.x, acc[h]);
-                    acc[h] = fmaf(kk.y, qq.y, acc[h]);
-                    acc[h] = fmaf(kk.z, qq.z, acc[h]);
-                    acc[h] = fmaf(kk.w, qq.w, acc[h]);
-                }
-            }
-#pragma unroll
-            for (int h = 0; h < GRP; ++h) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 16);
-            if (lane < 16) {
-                float* r = &sm.red[warp][qp][0];
-                *reinterpret_cast<float4*>(r) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-                *reinterpret_cast<float2*>(r + 4) = make_float2(acc[4], acc[5]);
-            }
-        }
-        __syncthreads();
-        // ---- online softmax (log2 units): threads 0..95 = (head h, position p)
-        if (tid < GRP * TILE) {
-            const int h = tid >> 4, p = tid & 15;
-            const bool valid = p < rows;
-            float s = (sm.red[0][p][h] + sm.red[1][p][h] + sm.red[2][p][h] + sm.red[3][p][h]) * LOG2E;
-            s = valid ? s : -INFINITY;
-            float tmax = s;
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
-            const float m_old = sm.m[h];
-            const float m_new = fmaxf(m_old, tmax);
-            const float alpha = exp2f(m_old - m_new);
-            const float pe = valid ? exp2f(s - m_new) : 0.0f;
-            float psum = pe;
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
-            sm.p[p][h] = pe;
-            if (p == 0) {
-                sm.m[h] = m_new;
-                sm.l[h] = sm.l[h] * alpha + psum;
-                sm.alpha[h] = alpha;
-            }
-        }
-        __syncthreads();
-        // ---- o = alpha*o + P V : thread owns dims 2*tid, 2*tid+1
-        {
+            const float* qs = q_buf + ((size_t)it.b * GRP * kvc + (size_t)it.kvh * GRP) * HD;
 #pragma unroll
             for (int h = 0; h < GRP; ++h) {
-                const float a = sm.alpha[h];
-                o[h][0] *= a;
-                o[h][1] *= a;
+                q[h][0] = *reinterpret_cast<const float4*>(qs + h * HD + 4 * lane);
+                q[h][1] = *reinterpret_cast<const float4*>(qs + h * HD + 128 + 4 * lane);
             }
-            for (int p = 0; p < rows; ++p) {
-                const float4 pa = *reinterpret_cast<const float4*>(&sm.p[p][0]);
-                const float2 pb = *reinterpret_cast<const float2*>(&sm.p[p][4]);
-                const float2 vv = *reinterpret_cast<const float2*>(&sm.v[stage][p][2 * tid]);
-                const float pp[GRP] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y};
+        }
+        float o[GRP][8];
+#pragma unroll
+        for (int h = 0; h < GRP; ++h)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[h][e] = 0.0f;
+        float m_run = -INFINITY, l_run = 0.0f;     // meaningful in lanes 0..5 (head = lane)
+
+        for (int t = 0; t < it.ntiles; ++t, ++j) {
+            const int stage = j % STAGES;
+            const int rows = min(TP, it.p1 - (it.p0 + t * TP));
+            if (!mbar_wait(&R.full[stage], (uint32_t)((j / STAGES) & 1), err)) return;
+            // ---- partial scores: part[p*6 + h] over this lane's 8 dims
+            float part[TP * GRP];
+#pragma unroll
+            for (int p = 0; p < TP; ++p) {
+                const float4 k0 = *reinterpret_cast<const float4*>(&R.k[stage][p][4 * lane]);
+                const float4 k1 = *reinterpret_cast<const float4*>(&R.k[stage][p][128 + 4 * lane]);
 #pragma unroll
                 for (int h = 0; h < GRP; ++h) {
-                    o[h][0] = fmaf(pp[h], vv.x, o[h][0]);
-                    o[h][1] = fmaf(pp[h], vv.y, o[h][1]);
+                    float a = k0.x * q[h][0].x;
+                    a = fmaf(k0.y, q[h][0].y, a);
+                    a = fmaf(k0.z, q[h][0].z, a);
+                    a = fmaf(k0.w, q[h][0].w, a);
+                    a = fmaf(k1.x, q[h][1].x, a);
+                    a = fmaf(k1.y, q[h][1].y, a);
+                    a = fmaf(k1.z, q[h][1].z, a);
+                    a = fmaf(k1.w, q[h][1].w, a);
+                    part[p * GRP + h] = a;
                 }
             }
-        }
-        __syncthreads();
-        if (warp == 0 && j + STAGES < ntiles) {
-            const int jn = j + STAGES;
-            const int rn = min(TILE, p1 - (p0 + jn * TILE));
-            issue_tile(sm, stage, rn, kbase + (size_t)jn * TILE * HD, vbase + (size_t)jn * TILE * HD, lane);
-        }
-    }
-    if (!ok) return;
-    float* po = part_o + (size_t)item * GRP * HD;
+            // ---- reduce-scatter 48 -> 3 per lane pair (indices 3*k_grp .. 3*k_grp+2)
+            float r24[24], r12[12], r6[6], r3[3];
+            rs_level<24>(part, r24, b4, 16);
+            rs_level<12>(r24, r12, b3, 8);
+            rs_level<6>(r12, r6, b2, 4);
+            rs_level<3>(r6, r3, b1, 2);
 #pragma unroll
-    for (int h = 0; h < GRP; ++h)
-        *reinterpret_cast<float2*>(po + h * HD + 2 * tid) = make_float2(o[h][0], o[h][1]);
-    if (tid < GRP) {
-        part_ml[((size_t)item * GRP + tid) * 2 + 0] = sm.m[tid];
-        part_ml[((size_t)item * GRP + tid) * 2 + 1] = sm.l[tid];
+            for (int i = 0; i < 3; ++i) r3[i] += __shfl_xor_sync(0xffffffffu, r3[i], 1);
+            if ((lane & 1) == 0) {
+#pragma unroll
+                for (int i = 0; i < 3; ++i) R.sc[my_pos][my_h0 + i] = r3[i] * LOG2E;
+            }
+            __syncwarp();
+            // ---- online softmax: lane h < 6 owns head h
+            if (lane < GRP) {
+                float s[TP];
+                float tmax = -INFINITY;
+#pragma unroll
+                for (int p = 0; p < TP; ++p) {
+                    s[p] = p < rows ? R.sc[p][lane] : -INFINITY;
+                    tmax = fmaxf(tmax, s[p]);
+                }
+                const float m_new = fmaxf(m_run, tmax);
+                const float alpha = exp2f(m_run - m_new);
+                float psum = 0.0f;
+#pragma unroll
+                for (int p = 0; p < TP; ++p) {
+                    const float pe = p < rows ? exp2f(s[p] - m_new) : 0.0f;
+                    R.p[p][lane] = pe;
+                    psum += pe;
+                }
+                l_run = l_run * alpha + psum;
+                m_run = m_new;
+                R.alpha[lane] = alpha;
+            }
+            __syncwarp();
+            // ---- o = alpha * o + P V
+            {
+                const float4 a03 = *reinterpret_cast<const float4*>(&R.alpha[0]);
+                const float2 a45 = *reinterpret_cast<const float2*>(&R.alpha[4]);
+                const float a[GRP] = {a03.x, a03.y, a03.z, a03.w, a45.x, a45.y};
+                if (a[0] != 1.0f || a[1] != 1.0f || a[2] != 1.0f || a[3] != 1.0f || a[4] != 1.0f || a[5] != 1.0f) {
+#pragma unroll
+                    for (int h = 0; h < GRP; ++h)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) o[h][e] *= a[h];
+                }
+#pragma unroll
+                for (int p = 0; p < TP; ++p) {
+                    if (p < rows) {
+                        const float4 pa = *reinterpret_cast<const float4*>(&R.p[p][0]);
+                        const float2 pb = *reinterpret_cast<const float2*>(&R.p[p][4]);
+                        const float pp[GRP] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y};
+                        const float4 v0 = *reinterpret_cast<const float4*>(&R.v[stage][p][4 * lane]);
+                        const float4 v1 = *reinterpret_cast<const float4*>(&R.v[stage][p][128 + 4 * lane]);
+                        const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                        for (int h = 0; h < GRP; ++h)
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) o[h][e] = fmaf(pp[h], vv[e], o[h][e]);
+                    }
+                }
+            }
+            __syncwarp();
+            produce(stage);
+        }
+        // ---- write this item's unnormalised partial
+        float* po = part_o + (size_t)item * GRP * HD;
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) {
+            *reinterpret_cast<float4*>(po + h * HD + 4 * lane) = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
+            *reinterpret_cast<float4*>(po + h * HD + 128 + 4 * lane) = make_float4(o[h][4], o[h][5], o[h][6], o[h][7]);
+        }
+        if (lane < GRP) {
+            part_ml[((size_t)item * GRP + lane) * 2 + 0] = m_run;
+            part_ml[((size_t)item * GRP + lane) * 2 + 1] = l_run;
+        }
     }
 }
 
@@ -307,8 +379,9 @@ cudaError_t launch_gqa_decode(dz_ctx* ctx, int layer, const GqaDecodeDesc& d, co
     cudaFuncSetAttribute(gqa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SplitSmem));
     gqa_prep_kernel<<<d.B, 256, 0, st>>>(d, kvc, L.d_kv, L.q_norm, L.k_norm, ctx->rope, q_gate, k, v, ctx->q_buf,
                                          ctx->cfg.rms_eps);
-    gqa_split_kernel<<<items, 128, sizeof(SplitSmem), st>>>(d, kvc, L.d_kv, ctx->q_buf, ctx->part_o, ctx->part_ml,
-                                                            ctx->d_err);
+    const int grid = std::min((items + NWARP - 1) / NWARP, ctx->n_sm);
+    gqa_split_kernel<<<grid, 32 * NWARP, sizeof(SplitSmem), st>>>(d, kvc, L.d_kv, ctx->q_buf, ctx->part_o,
+                                                                  ctx->part_ml, ctx->d_err, items);
     gqa_combine_kernel<<<dim3(kvc, d.B), 256, 0, st>>>(d, kvc, ctx->part_o, ctx->part_ml, q_gate, out);
     *n_launch += 3;
     return cudaGetLastError();
@@ -329,7 +402,9 @@ cudaError_t launch_gqa_decode_scratch(dz_ctx* ctx, int layer, const GqaDecodeDes
     cudaFuncSetAttribute(gqa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SplitSmem));
     gqa_prep_kernel<<<d.B, 256, 0, st>>>(d, kvc, L.d_kv, L.q_norm, L.k_norm, ctx->rope, q_gate, k, v, q_buf,
                                          ctx->cfg.rms_eps);
-    gqa_split_kernel<<<items, 128, sizeof(SplitSmem), st>>>(d, kvc, L.d_kv, q_buf, part_o, part_ml, ctx->d_err);
+    const int grid = std::min((items + NWARP - 1) / NWARP, ctx->n_sm);
+    gqa_split_kernel<<<grid, 32 * NWARP, sizeof(SplitSmem), st>>>(d, kvc, L.d_kv, q_buf, part_o, part_ml,
+                                                                  ctx->d_err, items);
     gqa_combine_kernel<<<dim3(kvc, d.B), 256, 0, st>>>(d, kvc, part_o, part_ml, q_gate, out);
     *n_launch += 3;
     return cudaGetLastError();
