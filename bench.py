@@ -349,6 +349,10 @@ def run_ours(args):
                "sample": f"8 of the 64 sequences (lengths {list(map(int, pick))}), {args.cpu_steps} decode step(s) "
                          f"of both layers, single thread like the reference's decode attention/scan; {dt:.2f} s"}
 
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill(dz, torch, local, args)
+
     err = ctx.device_error()
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -366,7 +370,7 @@ def run_ours(args):
                              "bytes_per_launch": gqa_b, "ms_per_launch": float(np.mean(gqa_ms))},
                 "gdn": {"achieved_gbs": gdn_gbs, "frac": gdn_gbs / hbm, "bytes": gdn_b,
                         "ms": float(np.mean(gdn_ms))},
-                "gpu_launches": launches, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu,
+                "gpu_launches": launches, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu, "prefill": prefill,
                 "device_error": err}
         if clk is None and clocks.raw:
             line["clocks_raw_head"] = clocks.raw[:300]
@@ -375,6 +379,54 @@ def run_ours(args):
     if dist:
         dist.destroy_process_group()
     return 0
+
+
+PF_T = 8192
+
+
+def run_prefill(dz, torch, local, args):
+    """Config 3 GQA prefill: one sequence, T=8192 bf16 tokens, positions 0..8191,
+    through dz_gqa_prefill_bf16 (prep + tcgen05 attention).  FLOPs counted as
+    4 * 24 * 256 * sum_{t<T}(t+1) (QK^T and PV over the causal range)."""
+    dev = torch.device("cuda", local)
+    cfg = dz.default_config(n_layers=2, full_attention_interval=2)
+    ctx = dz.Context(local, cfg)
+    (qn, kn), sp = layer_params(SEED0 + 3)
+    ctx.set_attn_params(1, qn, kn)
+    ctx.set_ssm_params(0, *sp)
+    ctx.cache_create([PF_T])
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED0 + 3)
+    qg = torch.randn(PF_T, HQ * 2 * HD, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(PF_T, HKV * HD, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(PF_T, HKV * HD, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(PF_T, HQ * HD, device=dev)
+    stream = torch.cuda.current_stream()
+    iters = max(3, args.prefill_iters)
+    for _ in range(3):
+        ctx.kv_truncate(1, 0, 0)
+        ctx.gqa_prefill(1, 0, qg, k, v, out)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        ctx.kv_truncate(1, 0, 0)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.gqa_prefill(1, 0, qg, k, v, out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    launches = ctx.last_launch_count
+    ctx.close()
+    flops = 4.0 * HQ * HD * (PF_T * (PF_T + 1) / 2)
+    ms = float(np.median(times))
+    tf = flops / (ms / 1000.0) / 1e12
+    _, bf16, kind = peaks()
+    return {"workload": "config 3 GQA prefill, T=8192, bf16 q/k/v, 24/4 heads, D=256, causal",
+            "ms": ms, "tflops": tf, "peak_tflops": bf16, "frac": tf / bf16, "peak_kind": f"{kind} bf16_tflops (burst)",
+            "flops": flops, "iters": iters, "launches_per_call": launches,
+            "timed": "dz_gqa_prefill_bf16 = prep (norm/rope/cache append) + tcgen05 attention, median of iters"}
 
 
 def main():
@@ -386,6 +438,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-steps", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-iters", type=int, default=5)
     ap.add_argument("--seqs", type=int, default=B_PER_RANK,
                     help="sequences per GPU (default 64 = config 2; smaller only for profiler captures)")
     args = ap.parse_args()

@@ -471,9 +471,32 @@ extern "C" int oc_gqa_decode(const float* q_gate, const float* k_in, const float
 //   q_gate [T][12288] (modified in place like the reference's qkv_buf),
 //   k, v [T][1024] (k modified in place), cos_sin [T][128] = cos[64] | sin[64].
 // ---------------------------------------------------------------------------
+static int gqa_prefill_impl(int64_t T, float* q_gate, float* k_buf, const float* v_buf, const float* q_norm,
+                            const float* k_norm, const float* cos_sin, float* kc, float* vc, int64_t cap,
+                            int64_t* len, float* out, int n_threads, const int64_t* rows, int64_t n_rows);
+
 extern "C" int oc_gqa_prefill(int64_t T, float* q_gate, float* k_buf, const float* v_buf,
                               const float* q_norm, const float* k_norm, const float* cos_sin,
                               float* kc, float* vc, int64_t cap, int64_t* len, float* out, int n_threads) {
+    return gqa_prefill_impl(T, q_gate, k_buf, v_buf, q_norm, k_norm, cos_sin, kc, vc, cap, len, out, n_threads,
+                            nullptr, 0);
+}
+
+// Same computation restricted to the (t, kvh) units of the listed tokens (every
+// K/V row is still normed, roped and appended): the per-unit arithmetic is the
+// reference's, so the listed rows equal oc_gqa_prefill's rows bit for bit.
+// out holds n_rows rows of 6144.
+extern "C" int oc_gqa_prefill_rows(int64_t T, float* q_gate, float* k_buf, const float* v_buf,
+                                   const float* q_norm, const float* k_norm, const float* cos_sin,
+                                   float* kc, float* vc, int64_t cap, int64_t* len, float* out, int n_threads,
+                                   const int64_t* rows, int64_t n_rows) {
+    return gqa_prefill_impl(T, q_gate, k_buf, v_buf, q_norm, k_norm, cos_sin, kc, vc, cap, len, out, n_threads,
+                            rows, n_rows);
+}
+
+static int gqa_prefill_impl(int64_t T, float* q_gate, float* k_buf, const float* v_buf, const float* q_norm,
+                            const float* k_norm, const float* cos_sin, float* kc, float* vc, int64_t cap,
+                            int64_t* len, float* out, int n_threads, const int64_t* rows, int64_t n_rows) {
     if (*len + T > cap) return 1;
     const int QS = HQ * 2 * HD, KS = HKV * HD, OS = HQ * HD;
     int64_t base_len = *len;
@@ -486,7 +509,7 @@ extern "C" int oc_gqa_prefill(int64_t T, float* q_gate, float* k_buf, const floa
         }
         kv_append(kc, vc, cap, len, kt, v_buf + t * KS);
     }
-    const int64_t n_units = T * HKV;
+    const int64_t n_units = (rows ? n_rows : T) * HKV;
     const float q_scale = 1.0f / sqrtf((float)HD);
     std::atomic<int64_t> next(0);
     auto worker = [&]() {
@@ -494,7 +517,8 @@ extern "C" int oc_gqa_prefill(int64_t T, float* q_gate, float* k_buf, const floa
             int64_t i = next.fetch_add(1);
             if (i >= n_units) break;
             int64_t rev = n_units - 1 - i;
-            int64_t t = rev / HKV;
+            int64_t ri = rev / HKV;
+            int64_t t = rows ? rows[ri] : ri;
             int kvh = (int)(rev % HKV);
             int64_t n_cached = base_len + t + 1;
             float* qt = q_gate + t * QS;
@@ -505,7 +529,7 @@ extern "C" int oc_gqa_prefill(int64_t T, float* q_gate, float* k_buf, const floa
                 apply_rope_partial(qh, ROPE, cs, cs + ROPE);
                 for (int d = 0; d < HD; d++) qh[d] *= q_scale;
             }
-            float* ot = out + t * OS;
+            float* ot = out + (rows ? ri : t) * OS;
             attend_kvh(kc, vc, cap, kvh, n_cached,
                        [&](int g) { return (const float*)(qt + (kvh * GRP + g) * 2 * HD); },
                        ot + kvh * GRP * HD);

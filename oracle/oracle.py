@@ -53,6 +53,9 @@ def lib():
                                     _f32p, _f32p, C.c_int64, C.POINTER(C.c_int64), _f32p]
         L.oc_gqa_prefill.argtypes = [C.c_int64, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
                                      _f32p, _f32p, C.c_int64, C.POINTER(C.c_int64), _f32p, C.c_int]
+        L.oc_gqa_prefill_rows.argtypes = [C.c_int64, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                          _f32p, _f32p, C.c_int64, C.POINTER(C.c_int64), _f32p, C.c_int, _i64p,
+                                          C.c_int64]
         L.oc_gdn_decode.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
                                     _f32p, _f32p, C.POINTER(C.c_int), _f32p]
         L.oc_gdn_prefill.argtypes = [C.c_int64, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
@@ -221,6 +224,27 @@ def gqa_prefill(q_gate, k, v, q_norm, k_norm, kv: OracleKv, start_pos=None, n_th
     rc = lib().oc_gqa_prefill(T, qg.reshape(-1), kk.reshape(-1), _c(v).reshape(-1), _c(q_norm), _c(k_norm),
                               cs.reshape(-1), kv.k.reshape(-1), kv.v.reshape(-1), kv.cap, C.byref(ln),
                               out.reshape(-1), nt)
+    if rc:
+        raise ValueError("kv cache full")
+    kv.len = ln.value
+    return out
+
+
+def gqa_prefill_rows(q_gate, k, v, q_norm, k_norm, kv: OracleKv, rows, n_threads=None):
+    """Parallel GQA prefill (model/forward.rs:599-721) evaluated only for the listed
+    tokens (all K/V rows are still appended).  Returns [len(rows), 6144]."""
+    T = q_gate.shape[0]
+    p0 = kv.len
+    cs = rope_table(np.arange(p0, p0 + T))
+    qg = _c(q_gate).copy()
+    kk = _c(k).copy()
+    ln = C.c_int64(kv.len)
+    rows = np.ascontiguousarray(rows, np.int64)
+    out = np.empty((rows.size, OUT_LEN), np.float32)
+    nt = n_threads or os.cpu_count() or 1
+    rc = lib().oc_gqa_prefill_rows(T, qg.reshape(-1), kk.reshape(-1), _c(v).reshape(-1), _c(q_norm), _c(k_norm),
+                                   cs.reshape(-1), kv.k.reshape(-1), kv.v.reshape(-1), kv.cap, C.byref(ln),
+                                   out.reshape(-1), nt, rows, rows.size)
     if rc:
         raise ValueError("kv cache full")
     kv.len = ln.value
