@@ -418,7 +418,37 @@ def run_prefill(dz, torch, local, args):
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1))
     launches = ctx.last_launch_count
+    # Gated DeltaNet prefill, same T: f32 qkv/alpha/beta/z, zero state and history
+    qkv = torch.randn(PF_T, QKV_LEN, device=dev, generator=g)
+    al = torch.randn(PF_T, SSM_HV, device=dev, generator=g)
+    be = torch.randn(PF_T, SSM_HV, device=dev, generator=g)
+    z = torch.randn(PF_T, INNER, device=dev, generator=g)
+    y = torch.empty(PF_T, INNER, device=dev)
+    zero_state = torch.zeros(SSM_HV, SSM_D, SSM_D, device=dev)
+    zero_hist = torch.zeros(4, QKV_LEN, device=dev)
+    gtimes = []
+    for it in range(3 + iters):
+        ctx.ssm_import(0, 0, zero_state, zero_hist, 0)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.gdn_prefill(0, 0, qkv, al, be, z, y)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if it >= 3:
+            gtimes.append(e0.elapsed_time(e1))
+    glaunches = ctx.last_launch_count
     ctx.close()
+    gms = float(np.median(gtimes))
+    C, d = 64, SSM_D
+    g_flops = (PF_T // C) * SSM_HV * (10 * C * C * d + 6 * C * d * d + (2 / 3) * C ** 3)
+    g_bytes = PF_T * (QKV_LEN + 2 * SSM_HV + 2 * INNER) * 4 + SSM_HV * SSM_D * SSM_D * 4 * 2
+    hbm, _, _ = peaks()
+    gdn = {"workload": "config 3 Gated DeltaNet prefill, T=8192, f32, chunk 64, zero state",
+           "ms": gms, "algorithmic_gflop": g_flops / 1e9, "tflops": g_flops / (gms / 1000.0) / 1e12,
+           "bytes": g_bytes, "gbs": g_bytes / (gms / 1000.0) / 1e9, "hbm_frac": g_bytes / (gms / 1000.0) / 1e9 / hbm,
+           "launches_per_call": glaunches,
+           "note": "f32 CUDA-core WY/UT chunk kernels (intra-chunk parallel, inter-chunk sequential per head)"}
     flops = 4.0 * HQ * HD * (PF_T * (PF_T + 1) / 2)
     ms = float(np.median(times))
     tf = flops / (ms / 1000.0) / 1e12
@@ -426,7 +456,8 @@ def run_prefill(dz, torch, local, args):
     return {"workload": "config 3 GQA prefill, T=8192, bf16 q/k/v, 24/4 heads, D=256, causal",
             "ms": ms, "tflops": tf, "peak_tflops": bf16, "frac": tf / bf16, "peak_kind": f"{kind} bf16_tflops (burst)",
             "flops": flops, "iters": iters, "launches_per_call": launches,
-            "timed": "dz_gqa_prefill_bf16 = prep (norm/rope/cache append) + tcgen05 attention, median of iters"}
+            "timed": "dz_gqa_prefill_bf16 = prep (norm/rope/cache append) + tcgen05 attention, median of iters",
+            "gdn": gdn}
 
 
 def main():

@@ -1,8 +1,401 @@
-// gdn_prefill.cu -- placeholder until the chunked Gated DeltaNet prefill lands.
+// gdn_prefill.cu -- chunked (C = 64) Gated DeltaNet prefill.
+//
+// Reference: Daiza-engine/src/model/forward.rs:897-1059 -- Phase A (conv1d from
+// in-batch rows or pre-batch ring slots (h0+t+ct+1)%4, SiLU, L2-norm q/k,
+// q *= 1/sqrt(128), silu(z)), the ring update (last min(4,T) rows, head =
+// (h0+T)%4), and Phase B: per v head a chain over t of the fused row pass
+// (model/ssm.rs:378-418) followed by the gated RMSNorm (ssm.rs:294-334).
+//
+// The token recurrence  S_t = e^{g_t} S_{t-1} + u_t k_t^T,
+//                        u_t = beta_t (v_t - e^{g_t} S_{t-1} k_t),  y_t = S_t q_t
+// is evaluated chunk by chunk (WY / UT form).  With G the in-chunk cumulative
+// log decay, Gam_ts = e^{G_t - G_s}, A = strict_lower(beta_t Gam_ts k_t.k_s) and
+// Tm = (I + A)^-1:
+//   U0 = Tm diag(beta) V,   W = Tm diag(beta e^G) K                (intra, parallel)
+//   U  = U0 - W S0^T
+//   Y  = diag(e^G) Q S0^T + (lower_incl(Gam) o Q K^T) U
+//   S_C = e^{G_last} S0 + U^T diag(e^{G_last - G}) K                 (inter, sequential)
+// All exponents are <= 0 (no overflow).  Kernels:
+//   gdn_pf_conv   per token: conv + SiLU + L2 norms + gates (log decay, beta)
+//   gdn_pf_ring   ring-buffer update (after every conv read)
+//   gdn_pf_intra  per (chunk, v head): G, K K^T, Q K^T, Tm by forward
+//                 substitution, W, U0, Q e^G, K e^{G_last-G}
+//   gdn_pf_inter  per (v head, 32-row block of S): the chunk recurrence
+//   gdn_pf_gate   per token: y * inv_rms * w * silu(z)
+#include <cstddef>
+
 #include "dz_internal.h"
+
 namespace dz {
-cudaError_t launch_gdn_prefill(dz_ctx*, int, int, int64_t, const float*, const float*, const float*, const float*,
-                               float*, cudaStream_t, int*) {
-    return cudaErrorNotSupported;
+
+namespace gp {
+constexpr int C = 64;            // chunk length
+constexpr int D = SSM_D;         // 128
+constexpr int KP = D + 4;        // padded smem row (floats) for 128-wide rows
+constexpr int MP = C + 1;        // padded smem row for 64x64 matrices
+constexpr int VB = 32;           // state rows per inter CTA
+// per (chunk, v head) record: X [128][128] (rows 0..63 = W, 64..127 = Q e^G),
+// U0 [64][128], Kd [64][128], P [64][64], eGl [4]
+constexpr size_t OFF_X = 0, OFF_U0 = OFF_X + 2 * C * D, OFF_KD = OFF_U0 + C * D, OFF_P = OFF_KD + C * D,
+                 OFF_EG = OFF_P + C * C, REC = OFF_EG + 4;
+}  // namespace gp
+
+// ---------------------------------------------------------------------------
+// Phase A: conv1d + SiLU + L2 norms + gates, one CTA per token
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) gdn_pf_conv_kernel(int64_t T, int vh0, int vc, int h0,
+                                                          const float* __restrict__ qkv,
+                                                          const float* __restrict__ hist,
+                                                          const float* __restrict__ conv_w,
+                                                          const float* __restrict__ ssm_a,
+                                                          const float* __restrict__ dt_bias,
+                                                          const float* __restrict__ alpha,
+                                                          const float* __restrict__ beta, float* __restrict__ qn,
+                                                          float* __restrict__ kn, float* __restrict__ vv,
+                                                          float* __restrict__ gl, float* __restrict__ bt) {
+    const int64_t t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float qscale = 1.0f / sqrtf((float)SSM_D);
+    for (int gi = warp; gi < 2 * SSM_HK + vc; gi += 8) {
+        int cb;
+        if (gi < SSM_HK) cb = gi * SSM_D;                               // q head
+        else if (gi < 2 * SSM_HK) cb = QKD + (gi - SSM_HK) * SSM_D;     // k head
+        else cb = 2 * QKD + (vh0 + gi - 2 * SSM_HK) * SSM_D;            // v head
+        const int ch = cb + 4 * lane;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int ct = 0; ct < CONV_K; ++ct) {
+            const int64_t st = t + ct - (CONV_K - 1);
+            const float* src = st >= 0 ? qkv + st * QKV_LEN
+                                       : hist + (size_t)((h0 + t + ct + 1) % CONV_K) * QKV_LEN;
+            const float4 x = *reinterpret_cast<const float4*>(src + ch);
+            const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)ct * QKV_LEN + ch);
+            acc.x = fmaf(x.x, w.x, acc.x);
+            acc.y = fmaf(x.y, w.y, acc.y);
+            acc.z = fmaf(x.z, w.z, acc.z);
+            acc.w = fmaf(x.w, w.w, acc.w);
+        }
+        acc = make_float4(siluf_acc(acc.x), siluf_acc(acc.y), siluf_acc(acc.z), siluf_acc(acc.w));
+        if (gi < 2 * SSM_HK) {
+            const float ss = warp_sum(acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w);
+            float inv = 1.0f / sqrtf(ss + 1e-6f);
+            const bool is_q = gi < SSM_HK;
+            const int kh = is_q ? gi : gi - SSM_HK;
+            acc = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            if (is_q) acc = make_float4(acc.x * qscale, acc.y * qscale, acc.z * qscale, acc.w * qscale);
+            float* dst = (is_q ? qn : kn) + ((size_t)t * SSM_HK + kh) * SSM_D;
+            reinterpret_cast<float4*>(dst)[lane] = acc;
+        } else {
+            const int vl = gi - 2 * SSM_HK;
+            reinterpret_cast<float4*>(vv + ((size_t)t * vc + vl) * SSM_D)[lane] = acc;
+        }
+    }
+    for (int vl = threadIdx.x; vl < vc; vl += blockDim.x) {
+        const int vh = vh0 + vl;
+        gl[(size_t)t * vc + vl] = ssm_a[vh] * softplus_ref(alpha[(size_t)t * SSM_HV + vh] + dt_bias[vh]);
+        bt[(size_t)t * vc + vl] = sigmoidf_acc(beta[(size_t)t * SSM_HV + vh]);
+    }
 }
+
+// ring update: the last m = min(4, T) raw rows land in slots (h0 + t) % 4
+__global__ void gdn_pf_ring_kernel(int64_t T, int h0, const float* __restrict__ qkv, float* __restrict__ hist) {
+    const int64_t m = T < CONV_K ? T : CONV_K;
+    const int64_t t = T - m + blockIdx.x;
+    const int slot = (int)((h0 + t) % CONV_K);
+    for (int c = threadIdx.x; c < QKV_LEN / 4; c += blockDim.x)
+        reinterpret_cast<float4*>(hist + (size_t)slot * QKV_LEN)[c] =
+            reinterpret_cast<const float4*>(qkv + (size_t)t * QKV_LEN)[c];
+}
+
+// ---------------------------------------------------------------------------
+// intra-chunk WY transform, one CTA per (chunk, local v head)
+// ---------------------------------------------------------------------------
+struct IntraSmem {
+    float K[gp::C][gp::KP];
+    float Q[gp::C][gp::KP];
+    float V[gp::C][gp::KP];
+    float M1[gp::C][gp::MP];   // K K^T -> A
+    float M2[gp::C][gp::MP];   // Q K^T -> Tm
+    float g[gp::C], G[gp::C], b[gp::C], eG[gp::C];
+};
+
+__global__ void __launch_bounds__(256) gdn_pf_intra_kernel(int64_t T, int vh0, int vc, const float* __restrict__ qn,
+                                                           const float* __restrict__ kn, const float* __restrict__ vv,
+                                                           const float* __restrict__ gl, const float* __restrict__ bt,
+                                                           float* __restrict__ rec) {
+    using namespace gp;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    IntraSmem& sm = *reinterpret_cast<IntraSmem*>(smem_raw);
+    const int c = blockIdx.x, vl = blockIdx.y, tid = threadIdx.x;
+    const int vh = vh0 + vl, kh = vh % SSM_HK;
+    const int64_t t0 = (int64_t)c * C;
+    const int n = (int)(T - t0 < C ? T - t0 : C);
+    float* out = rec + ((size_t)c * vc + vl) * REC;
+
+    // load K, Q, V (zero rows past n), g, beta
+    for (int i = tid; i < C * (D / 4); i += 256) {
+        const int r = i / (D / 4), c4 = i % (D / 4);
+        float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = k4, v4 = k4;
+        if (r < n) {
+            k4 = reinterpret_cast<const float4*>(kn + ((size_t)(t0 + r) * SSM_HK + kh) * D)[c4];
+            q4 = reinterpret_cast<const float4*>(qn + ((size_t)(t0 + r) * SSM_HK + kh) * D)[c4];
+            v4 = reinterpret_cast<const float4*>(vv + ((size_t)(t0 + r) * vc + vl) * D)[c4];
+        }
+        *reinterpret_cast<float4*>(&sm.K[r][4 * c4]) = k4;
+        *reinterpret_cast<float4*>(&sm.Q[r][4 * c4]) = q4;
+        *reinterpret_cast<float4*>(&sm.V[r][4 * c4]) = v4;
+    }
+    if (tid < C) {
+        sm.g[tid] = tid < n ? gl[(size_t)(t0 + tid) * vc + vl] : 0.0f;
+        sm.b[tid] = tid < n ? bt[(size_t)(t0 + tid) * vc + vl] : 0.0f;
+    }
+    __syncthreads();
+    if (tid < 32) {   // inclusive cumsum of 64 log decays
+        float a0 = sm.g[2 * tid], a1 = sm.g[2 * tid + 1];
+        float s = a0 + a1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, s, o);
+            if (tid >= o) s += y;
+        }
+        const float excl = s - (a0 + a1);
+        sm.G[2 * tid] = excl + a0;
+        sm.G[2 * tid + 1] = excl + a0 + a1;
+    }
+    __syncthreads();
+    if (tid < C) sm.eG[tid] = expf(sm.G[tid]);
+    // K K^T and Q K^T: thread -> row i, 16 columns
+    {
+        const int i = tid >> 2, j0 = (tid & 3) * 16;
+        float akk[16], aqk[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) { akk[jj] = 0.f; aqk[jj] = 0.f; }
+        for (int kk = 0; kk < D; kk += 4) {
+            const float4 ki = *reinterpret_cast<const float4*>(&sm.K[i][kk]);
+            const float4 qi = *reinterpret_cast<const float4*>(&sm.Q[i][kk]);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+                const float4 kj = *reinterpret_cast<const float4*>(&sm.K[j0 + jj][kk]);
+                akk[jj] = fmaf(ki.x, kj.x, fmaf(ki.y, kj.y, fmaf(ki.z, kj.z, fmaf(ki.w, kj.w, akk[jj]))));
+                aqk[jj] = fmaf(qi.x, kj.x, fmaf(qi.y, kj.y, fmaf(qi.z, kj.z, fmaf(qi.w, kj.w, aqk[jj]))));
+            }
+        }
+        __syncthreads();
+        const float Gi = sm.G[i], bi = sm.b[i];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+            const int j = j0 + jj;
+            const float gam = (j <= i) ? expf(Gi - sm.G[j]) : 0.0f;
+            sm.M1[i][j] = (j < i) ? bi * gam * akk[jj] : 0.0f;          // A
+            out[OFF_P + i * C + j] = (j <= i) ? gam * aqk[jj] : 0.0f;   // P
+        }
+    }
+    __syncthreads();
+    // Tm = (I + A)^-1 by forward substitution, row by row; column j by thread j
+    for (int i = 0; i < C; ++i) {
+        if (tid < C) {
+            const int j = tid;
+            float x = (i == j) ? 1.0f : 0.0f;
+            if (j < i) {
+                for (int s = j; s < i; ++s) x = fmaf(-sm.M1[i][s], sm.M2[s][j], x);
+            }
+            sm.M2[i][j] = (j <= i) ? x : 0.0f;
+        }
+        __syncthreads();
+    }
+    // W = Tm diag(beta e^G) K, U0 = Tm diag(beta) V: thread -> row i, 32 columns
+    {
+        const int i = tid >> 2, k0 = (tid & 3) * 32;
+        float w[32], u[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) { w[e] = 0.f; u[e] = 0.f; }
+        for (int s = 0; s <= i; ++s) {
+            const float tb = sm.M2[i][s] * sm.b[s];
+            const float tbe = tb * sm.eG[s];
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(&sm.K[s][k0 + e]);
+                const float4 v4 = *reinterpret_cast<const float4*>(&sm.V[s][k0 + e]);
+                w[e] = fmaf(tbe, k4.x, w[e]); w[e + 1] = fmaf(tbe, k4.y, w[e + 1]);
+                w[e + 2] = fmaf(tbe, k4.z, w[e + 2]); w[e + 3] = fmaf(tbe, k4.w, w[e + 3]);
+                u[e] = fmaf(tb, v4.x, u[e]); u[e + 1] = fmaf(tb, v4.y, u[e + 1]);
+                u[e + 2] = fmaf(tb, v4.z, u[e + 2]); u[e + 3] = fmaf(tb, v4.w, u[e + 3]);
+            }
+        }
+        const float eGi = sm.eG[i];
+        const float gl_last = sm.G[n - 1];
+        const float ed = expf(gl_last - sm.G[i]);
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+            *reinterpret_cast<float4*>(out + OFF_X + (size_t)i * D + k0 + e) = make_float4(w[e], w[e + 1], w[e + 2], w[e + 3]);
+            *reinterpret_cast<float4*>(out + OFF_U0 + (size_t)i * D + k0 + e) = make_float4(u[e], u[e + 1], u[e + 2], u[e + 3]);
+            const float4 q4 = *reinterpret_cast<const float4*>(&sm.Q[i][k0 + e]);
+            *reinterpret_cast<float4*>(out + OFF_X + (size_t)(C + i) * D + k0 + e) =
+                make_float4(q4.x * eGi, q4.y * eGi, q4.z * eGi, q4.w * eGi);
+            const float4 k4 = *reinterpret_cast<const float4*>(&sm.K[i][k0 + e]);
+            *reinterpret_cast<float4*>(out + OFF_KD + (size_t)i * D + k0 + e) =
+                make_float4(k4.x * ed, k4.y * ed, k4.z * ed, k4.w * ed);
+        }
+        if (tid == 0) out[OFF_EG] = expf(gl_last);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// inter-chunk recurrence: one CTA per (32-row block of S, local v head)
+// ---------------------------------------------------------------------------
+struct InterSmem {
+    float S[gp::VB][gp::KP];     // state rows [v][k]
+    float U[gp::C][gp::VB + 1];
+    float Yp[gp::C][gp::VB + 1];
+};
+
+__global__ void __launch_bounds__(256) gdn_pf_inter_kernel(int64_t T, int vc, const float* __restrict__ rec,
+                                                           float* __restrict__ state, float* __restrict__ yraw) {
+    using namespace gp;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    InterSmem& sm = *reinterpret_cast<InterSmem*>(smem_raw);
+    const int vb = blockIdx.x, vl = blockIdx.y, tid = threadIdx.x;
+    float* Sg = state + ((size_t)vl * D + (size_t)vb * VB) * D;
+    for (int i = tid; i < VB * (D / 4); i += 256) {
+        const int r = i / (D / 4), c4 = i % (D / 4);
+        *reinterpret_cast<float4*>(&sm.S[r][4 * c4]) = reinterpret_cast<const float4*>(Sg + (size_t)r * D)[c4];
+    }
+    __syncthreads();
+    const int NC = (int)((T + C - 1) / C);
+    for (int c = 0; c < NC; ++c) {
+        const float* R = rec + ((size_t)c * vc + vl) * REC;
+        const int64_t t0 = (int64_t)c * C;
+        const int n = (int)(T - t0 < C ? T - t0 : C);
+        // step 1: [W; Q e^G] S^T  -> U = U0 - W S^T, Yp = Q e^G S^T
+        {
+            const int r = tid >> 1, v0 = (tid & 1) * 16;
+            float acc[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+            const float* xr = R + OFF_X + (size_t)r * D;
+            for (int k = 0; k < D; k += 4) {
+                const float4 x4 = __ldg(reinterpret_cast<const float4*>(xr + k));
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float4 s4 = *reinterpret_cast<const float4*>(&sm.S[v0 + e][k]);
+                    acc[e] = fmaf(x4.x, s4.x, fmaf(x4.y, s4.y, fmaf(x4.z, s4.z, fmaf(x4.w, s4.w, acc[e]))));
+                }
+            }
+            if (r < C) {
+                const float* u0 = R + OFF_U0 + (size_t)r * D + vb * VB + v0;
+#pragma unroll
+                for (int e = 0; e < 16; ++e) sm.U[r][v0 + e] = __ldg(u0 + e) - acc[e];
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) sm.Yp[r - C][v0 + e] = acc[e];
+            }
+        }
+        __syncthreads();
+        // step 2: Y = Yp + P U (P lower-triangular incl. diagonal)
+        {
+            const int i = tid >> 2, v0 = (tid & 3) * 8;
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) y[e] = sm.Yp[i][v0 + e];
+            const float* pr = R + OFF_P + (size_t)i * C;
+            for (int s = 0; s <= i; ++s) {
+                const float p = __ldg(pr + s);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[e] = fmaf(p, sm.U[s][v0 + e], y[e]);
+            }
+            if (i < n) {
+                float* yo = yraw + ((size_t)(t0 + i) * vc + vl) * D + vb * VB + v0;
+                *reinterpret_cast<float4*>(yo) = make_float4(y[0], y[1], y[2], y[3]);
+                *reinterpret_cast<float4*>(yo + 4) = make_float4(y[4], y[5], y[6], y[7]);
+            }
+        }
+        // step 3: S = e^{G_last} S + U^T Kd   (reads U, writes S; step-1 reads of S are done)
+        {
+            const int v = tid >> 3, k0 = (tid & 7) * 16;
+            const float eGl = __ldg(R + OFF_EG);
+            float acc[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[e] = eGl * sm.S[v][k0 + e];
+            const float* kd = R + OFF_KD + k0;
+            for (int s = 0; s < n; ++s) {
+                const float u = sm.U[s][v];
+#pragma unroll
+                for (int e = 0; e < 16; e += 4) {
+                    const float4 k4 = __ldg(reinterpret_cast<const float4*>(kd + (size_t)s * D + e));
+                    acc[e] = fmaf(u, k4.x, acc[e]);
+                    acc[e + 1] = fmaf(u, k4.y, acc[e + 1]);
+                    acc[e + 2] = fmaf(u, k4.z, acc[e + 2]);
+                    acc[e + 3] = fmaf(u, k4.w, acc[e + 3]);
+                }
+            }
+            __syncthreads();   // every thread finished reading S (step 1) and U (steps 2, 3)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) sm.S[v][k0 + e] = acc[e];
+        }
+        __syncthreads();
+    }
+    for (int i = tid; i < VB * (D / 4); i += 256) {
+        const int r = i / (D / 4), c4 = i % (D / 4);
+        reinterpret_cast<float4*>(Sg + (size_t)r * D)[c4] = *reinterpret_cast<const float4*>(&sm.S[r][4 * c4]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// gated RMSNorm (prefill variant, ss / head_dim; ssm.rs:294-334), per token
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) gdn_pf_gate_kernel(int vh0, int vc, const float* __restrict__ yraw,
+                                                          const float* __restrict__ z,
+                                                          const float* __restrict__ norm_w,
+                                                          float* __restrict__ y_out) {
+    const int64_t t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float4 w = reinterpret_cast<const float4*>(norm_w)[lane];
+    for (int vl = warp; vl < vc; vl += 8) {
+        const float4 y = reinterpret_cast<const float4*>(yraw + ((size_t)t * vc + vl) * SSM_D)[lane];
+        const float ss = warp_sum(y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w);
+        const float inv = 1.0f / sqrtf(ss / (float)SSM_D + 1e-6f);
+        const float4 zz = reinterpret_cast<const float4*>(z + (size_t)t * INNER + (size_t)(vh0 + vl) * SSM_D)[lane];
+        float4 o;
+        o.x = ((y.x * inv) * w.x) * siluf_acc(zz.x);
+        o.y = ((y.y * inv) * w.y) * siluf_acc(zz.y);
+        o.z = ((y.z * inv) * w.z) * siluf_acc(zz.z);
+        o.w = ((y.w * inv) * w.w) * siluf_acc(zz.w);
+        reinterpret_cast<float4*>(y_out + ((size_t)t * vc + vl) * SSM_D)[lane] = o;
+    }
+}
+
+cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* qkv, const float* alpha,
+                               const float* beta, const float* z, float* y, cudaStream_t st, int* n_launch) {
+    using namespace gp;
+    const LayerState& L = ctx->layers[layer];
+    const int vh0 = ctx->cfg.v_head_begin, vc = ctx->cfg.v_head_count;
+    const SsmSlot slot = L.h_ssm[seq];
+    const int h0 = L.head[seq];
+    const int NC = (int)((T + C - 1) / C);
+    const size_t n_qk = (size_t)T * SSM_HK * D, n_v = (size_t)T * vc * D, n_g = (size_t)T * vc;
+    const size_t n_rec = (size_t)NC * vc * REC;
+    const size_t total = 2 * n_qk + 2 * n_v + 2 * n_g + n_rec + 64;
+    cudaError_t e = ensure_prefill_scratch(ctx, total * sizeof(float));
+    if (e != cudaSuccess) return e;
+    float* qn = static_cast<float*>(ctx->pf);
+    float* kn = qn + n_qk;
+    float* vv = kn + n_qk;
+    float* yraw = vv + n_v;
+    float* gl = yraw + n_v;
+    float* bt = gl + n_g;
+    float* rec = bt + n_g;
+    rec = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(rec) + 15) & ~uintptr_t(15));
+
+    gdn_pf_conv_kernel<<<(unsigned)T, 256, 0, st>>>(T, vh0, vc, h0, qkv, slot.hist, L.conv_w, L.ssm_a, L.dt_bias,
+                                                    alpha, beta, qn, kn, vv, gl, bt);
+    gdn_pf_ring_kernel<<<(unsigned)(T < CONV_K ? T : CONV_K), 256, 0, st>>>(T, h0, qkv, slot.hist);
+    cudaFuncSetAttribute(gdn_pf_intra_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(IntraSmem));
+    gdn_pf_intra_kernel<<<dim3(NC, vc), 256, sizeof(IntraSmem), st>>>(T, vh0, vc, qn, kn, vv, gl, bt, rec);
+    cudaFuncSetAttribute(gdn_pf_inter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(InterSmem));
+    gdn_pf_inter_kernel<<<dim3(D / VB, vc), 256, sizeof(InterSmem), st>>>(T, vc, rec, slot.state, yraw);
+    gdn_pf_gate_kernel<<<(unsigned)T, 256, 0, st>>>(vh0, vc, yraw, z, L.norm_w, y);
+    *n_launch += 5;
+    return cudaGetLastError();
+}
+
 }  // namespace dz
