@@ -460,6 +460,114 @@ def run_prefill(dz, torch, local, args):
             "gdn": gdn}
 
 
+def run_stack(args):
+    """Config 4: the 64-layer attention stack (48 Gated DeltaNet + 16 GQA layers),
+    head-sharded over the ranks with an NCCL all-gather of head outputs after
+    every layer.  Decode: batch 8 at context 131072 (KV rows are a synthetic byte
+    pattern).  Prefill: one sequence of 32768 tokens."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from daiza_b200 import parallel as P
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29555")
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    B, CTX, T = 8, args.stack_ctx, args.stack_prefill
+    steps, warm = args.steps, args.warmup
+    plan = P.head_plan(world, rank)
+    rows = plan.decode_rows(B)
+    caps = [(CTX + steps + warm + 2) if b in rows else 1 for b in range(B)] + [T]
+
+    def params(layer, kind):
+        a, s_ = layer_params(SEED0 + 4 * 1000 + layer)
+        return a if kind == "attn" else s_
+
+    stack = P.ShardedStack(local, B, caps, params)
+    t0 = time.time()
+    for layer in range(64):
+        if stack.ctx.is_attention(layer):
+            for b in rows:
+                stack.ctx.kv_fill_pattern(layer, b, CTX, 0x3C)
+    torch.cuda.synchronize()
+    fill_s = time.time() - t0
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED0 + 4)
+    qg = torch.randn(B, HQ * 2 * HD, device=dev, generator=g)
+    k = torch.randn(B, HKV * HD, device=dev, generator=g)
+    v = torch.randn(B, HKV * HD, device=dev, generator=g)
+    gdn = tuple(torch.randn(B, n, device=dev, generator=g) for n in (QKV_LEN, SSM_HV, SSM_HV, INNER))
+    sq, sk, sv = stack.slice_inputs(qg, k, v)
+    gqa_in = tuple(x[rows[0]:rows[-1] + 1].contiguous() for x in (sq, sk, sv))
+    stream = torch.cuda.current_stream()
+    for _ in range(warm):
+        stack.decode_step(gqa_in, gdn)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        stack.decode_step(gqa_in, gdn)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    dms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    dist.all_reduce(dms, op=dist.ReduceOp.MAX)
+    dms = float(dms.item())
+    # bytes per decode step on this rank: its KV rows (incl. new token) + its DeltaNet states
+    ctx_now = CTX + warm + steps // 2
+    kvc = plan.kv_heads[1] - plan.kv_heads[0]
+    vc = plan.v_heads[1] - plan.v_heads[0]
+    rank_bytes = 16 * len(rows) * (ctx_now + 1) * kvc * HD * 4 * 2 + 48 * B * vc * SSM_D * SSM_D * 4 * 2
+    hbm, bf16, kind = peaks()
+    # prefill
+    pg = torch.randn(T, HQ * 2 * HD, device=dev, generator=g).to(torch.bfloat16)
+    pk = torch.randn(T, HKV * HD, device=dev, generator=g).to(torch.bfloat16)
+    pv = torch.randn(T, HKV * HD, device=dev, generator=g).to(torch.bfloat16)
+    pgdn = tuple(torch.randn(T, n, device=dev, generator=g) for n in (QKV_LEN, SSM_HV, SSM_HV, INNER))
+    pin = stack.slice_inputs(pg, pk, pv)
+    ptimes = []
+    for it in range(1 + args.stack_prefill_iters):
+        stack.ctx.cache_reset(B)
+        torch.cuda.synchronize()
+        dist.barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        stack.prefill(B, pin, pgdn)
+        a1.record(stream)
+        torch.cuda.synchronize()
+        if it > 0:
+            ptimes.append(a0.elapsed_time(a1))
+    pms = torch.tensor([float(np.median(ptimes))], device=dev)
+    dist.all_reduce(pms, op=dist.ReduceOp.MAX)
+    pms = float(pms.item())
+    gqa_flops = 16 * 4.0 * HQ * HD * (T * (T + 1) / 2)
+    err = stack.ctx.device_error()
+    stack.close()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "workload": "config 4: 64-layer stack (48 GDN + 16 GQA), head-sharded, NCCL all-gather "
+                                          "of head outputs per layer",
+            "n_gpus": world, "scaling": "strong",
+            "decode": {"batch": B, "context": CTX, "ms_per_token_step": dms, "tok_s": B / (dms / 1000.0),
+                       "hbm_gbs_per_gpu": rank_bytes / (dms / 1000.0) / 1e9,
+                       "hbm_frac_per_gpu": rank_bytes / (dms / 1000.0) / 1e9 / hbm, "steps": steps, "warmup": warm,
+                       "kv": "synthetic byte pattern (0x3C) for the cached rows"},
+            "prefill": {"tokens": T, "ms": pms, "tok_s": T / (pms / 1000.0),
+                        "gqa_tflops_whole_job": gqa_flops / (pms / 1000.0) / 1e12,
+                        "note": "ms covers all 64 layers incl. per-layer all-gathers (GQA + GDN)"},
+            "plan": {"kv_heads_per_rank": kvc, "v_heads_per_rank": vc, "pair_count": plan.pair_count},
+            "kv_fill_s": fill_s, "device_error": err}))
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -470,6 +578,11 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "stack"],
+                    help="decode = config 2 (the bench line); stack = config 4 (64 layers, head-sharded)")
+    ap.add_argument("--stack-ctx", type=int, default=131072)
+    ap.add_argument("--stack-prefill", type=int, default=32768)
+    ap.add_argument("--stack-prefill-iters", type=int, default=2)
     ap.add_argument("--prefill-iters", type=int, default=5)
     ap.add_argument("--seqs", type=int, default=B_PER_RANK,
                     help="sequences per GPU (default 64 = config 2; smaller only for profiler captures)")
@@ -478,6 +591,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "stack":
+        return run_stack(args)
     return run_ours(args)
 
 

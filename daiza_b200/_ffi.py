@@ -26,7 +26,7 @@ class dz_config(C.Structure):
                [("rope_freq_base", C.c_float), ("rms_eps", C.c_float)] + \
                [(n, C.c_int32) for n in ("ssm_conv_kernel", "ssm_state_size", "ssm_group_count",
                                          "ssm_time_step_rank", "ssm_inner_size", "kv_head_begin", "kv_head_count",
-                                         "v_head_begin", "v_head_count")]
+                                         "v_head_begin", "v_head_count", "qtile_split_index", "qtile_split_count")]
 
 
 _P = C.c_void_p
@@ -51,6 +51,7 @@ SIGNATURES = {
     "dz_ssm_export": [_P, _I, _I, _P, _P, C.POINTER(C.c_int32)],
     "dz_ssm_import": [_P, _I, _I, _P, _P, C.c_int32],
     "dz_rope_table": [_P, _I64, _I64, _P],
+    "dz_kv_fill_pattern": [_P, _I, _I, _I64, _I],
     "dz_gqa_decode": [_P, _I, _I, _P, _P, _P, _P, _P, _P],
     "dz_gdn_decode": [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P],
     "dz_gqa_prefill_bf16": [_P, _I, _I, _I64, _P, _P, _P, _P, _P],

@@ -114,6 +114,8 @@ dz_status check_config(dz_ctx* ctx, const dz_config& c) {
     if (c.v_head_begin < 0 || c.v_head_count <= 0 || c.v_head_begin + c.v_head_count > SSM_HV)
         return fail(ctx, DZ_EINVAL, "v head slice [%d,%d) out of range", c.v_head_begin,
                     c.v_head_begin + c.v_head_count);
+    if (c.qtile_split_count < 1 || c.qtile_split_index < 0 || c.qtile_split_index >= c.qtile_split_count)
+        return fail(ctx, DZ_EINVAL, "query-tile split %d of %d invalid", c.qtile_split_index, c.qtile_split_count);
     return DZ_OK;
 }
 
@@ -179,6 +181,8 @@ dz_status dz_config_default(dz_config* c) {
     c->kv_head_count = HKV;
     c->v_head_begin = 0;
     c->v_head_count = SSM_HV;
+    c->qtile_split_index = 0;
+    c->qtile_split_count = 1;
     return DZ_OK;
 }
 
@@ -466,6 +470,21 @@ dz_status dz_ssm_import(dz_ctx* ctx, int layer, int seq, const float* state, con
     if (conv_history)
         DZ_CUDA(cudaMemcpy(L.h_ssm[seq].hist, conv_history, (size_t)CONV_K * QKV_LEN * 4, cudaMemcpyDefault));
     L.head[seq] = conv_head;
+    return DZ_OK;
+}
+
+dz_status dz_kv_fill_pattern(dz_ctx* ctx, int layer, int seq, int64_t len, int byte_value) {
+    if (!layer_ok(ctx, layer) || !ctx->layers[layer].is_attn || seq < 0 || seq >= ctx->n_seqs || len < 0)
+        return fail(ctx, DZ_EINVAL, "bad fill arguments");
+    LayerState& L = ctx->layers[layer];
+    if (len > L.h_kv[seq].cap) return fail(ctx, DZ_ESTATE, "fill of %lld rows exceeds capacity", (long long)len);
+    DeviceGuard g(ctx->device);
+    const int kvc = ctx->cfg.kv_head_count;
+    for (int h = 0; h < kvc && len > 0; ++h) {
+        DZ_CUDA(cudaMemset(L.h_kv[seq].k + (size_t)h * L.h_kv[seq].cap * HD, byte_value, (size_t)len * HD * 4));
+        DZ_CUDA(cudaMemset(L.h_kv[seq].v + (size_t)h * L.h_kv[seq].cap * HD, byte_value, (size_t)len * HD * 4));
+    }
+    L.len[seq] = len;
     return DZ_OK;
 }
 

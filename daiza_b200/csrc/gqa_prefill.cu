@@ -267,7 +267,8 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
                                                                    const __grid_constant__ CUtensorMap tm_v,
                                                                    int kvc, int64_t T, int64_t base,
                                                                    const Tg* __restrict__ q_gate,
-                                                                   float* __restrict__ out, int* err) {
+                                                                   float* __restrict__ out, int* err,
+                                                                   int split_idx, int split_cnt) {
     using namespace pf;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // dynamic smem is only guaranteed 16-byte aligned: round up to 1 KB
@@ -275,8 +276,10 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nq = GRP * kvc;
     const int n_qt = (int)((T + BM - 1) / BM);
-    // heaviest (latest) query tiles first
-    const int qt = n_qt - 1 - (int)(blockIdx.x / nq);
+    // heaviest (latest) query tiles first; with a split, this context owns the
+    // tiles qt % split_cnt == split_idx (interleaved: balanced causal work)
+    const int last_own = (n_qt - 1) - (((n_qt - 1) % split_cnt) - split_idx + split_cnt) % split_cnt;
+    const int qt = last_own - split_cnt * (int)(blockIdx.x / nq);
     const int qh = (int)(blockIdx.x % nq);
     const int kvh = qh / GRP;
     const int64_t q0 = (int64_t)qt * BM;
@@ -525,15 +528,19 @@ cudaError_t launch_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
     if (!make_map(&mq, qb, T, nq, pf::BM) || !make_map(&mk, kb, L, kvc, pf::BN) || !make_map(&mv, vb, L, kvc, pf::BN))
         return cudaErrorInvalidValue;
     const int n_qt = (int)((T + pf::BM - 1) / pf::BM);
+    const int sc = ctx->cfg.qtile_split_count, si = ctx->cfg.qtile_split_index;
+    const int n_own = n_qt > si ? (n_qt - 1 - si) / sc + 1 : 0;
     const size_t smem = sizeof(pf::Smem) + 1024;
     if (bf) {
         cudaFuncSetAttribute(pf_attn_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        pf_attn_kernel<__nv_bfloat16><<<n_qt * nq, pf::NTHREADS, smem, st>>>(
-            mq, mk, mv, kvc, T, base, reinterpret_cast<const __nv_bfloat16*>(q_gate), out, ctx->d_err);
+        if (n_own > 0)
+            pf_attn_kernel<__nv_bfloat16><<<n_own * nq, pf::NTHREADS, smem, st>>>(
+                mq, mk, mv, kvc, T, base, reinterpret_cast<const __nv_bfloat16*>(q_gate), out, ctx->d_err, si, sc);
     } else {
         cudaFuncSetAttribute(pf_attn_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        pf_attn_kernel<float><<<n_qt * nq, pf::NTHREADS, smem, st>>>(mq, mk, mv, kvc, T, base, q_gate_f, out,
-                                                                     ctx->d_err);
+        if (n_own > 0)
+            pf_attn_kernel<float><<<n_own * nq, pf::NTHREADS, smem, st>>>(mq, mk, mv, kvc, T, base, q_gate_f, out,
+                                                                         ctx->d_err, si, sc);
     }
     *n_launch += 1;
     return cudaGetLastError();

@@ -43,8 +43,9 @@ def _stream(stream):
     return C.c_void_p(s.cuda_stream)
 
 
-def default_config(n_layers=64, full_attention_interval=4, kv_heads=None, v_heads=None):
-    """Config::default (config.rs:47-74) with an optional head slice."""
+def default_config(n_layers=64, full_attention_interval=4, kv_heads=None, v_heads=None, qtile_split=None):
+    """Config::default (config.rs:47-74) with an optional head slice and
+    GQA-prefill query-tile split (index, count)."""
     cfg = _ffi.dz_config()
     check(_ffi.lib().dz_config_default(C.byref(cfg)))
     cfg.n_layers = n_layers
@@ -53,6 +54,8 @@ def default_config(n_layers=64, full_attention_interval=4, kv_heads=None, v_head
         cfg.kv_head_begin, cfg.kv_head_count = kv_heads[0], kv_heads[1] - kv_heads[0]
     if v_heads is not None:
         cfg.v_head_begin, cfg.v_head_count = v_heads[0], v_heads[1] - v_heads[0]
+    if qtile_split is not None:
+        cfg.qtile_split_index, cfg.qtile_split_count = qtile_split
     return cfg
 
 
@@ -156,6 +159,10 @@ class Context:
         s = np.ascontiguousarray(state, np.float32)
         hst = np.ascontiguousarray(conv_history, np.float32)
         self._chk(self.lib.dz_ssm_import(self.h, layer, seq, _np_ptr(s), _np_ptr(hst), int(conv_head)))
+
+    def kv_fill_pattern(self, layer, seq, length, byte_value=0x3C):
+        """Synthetic KV rows (benchmarks): every byte of rows [0, length) = byte_value."""
+        self._chk(self.lib.dz_kv_fill_pattern(self.h, layer, seq, int(length), int(byte_value)))
 
     def rope_table(self, pos0, n):
         out = np.zeros((n, 2 * ROPE), np.float32)

@@ -61,6 +61,11 @@ typedef struct dz_config {
     /* head slice owned by this context (head sharding); defaults: everything */
     int32_t kv_head_begin, kv_head_count;   /* GQA kv heads [begin, begin+count) */
     int32_t v_head_begin, v_head_count;     /* GDN v heads  [begin, begin+count) */
+    /* GQA prefill computes only the 128-token query tiles t with
+     * t % qtile_split_count == qtile_split_index (default 0 of 1 = all); the
+     * rows of other tiles are left untouched.  Lets two contexts share one kv
+     * head (8-way head sharding of 4 kv heads). */
+    int32_t qtile_split_index, qtile_split_count;
 } dz_config;
 
 /* Fills the Bonsai-27B defaults (Config::default, config.rs:47-74). */
@@ -109,6 +114,10 @@ dz_status dz_kv_import(dz_ctx* ctx, int layer, int seq, const float* k_flat, con
 dz_status dz_ssm_export(dz_ctx* ctx, int layer, int seq, float* state, float* conv_history, int32_t* conv_head);
 dz_status dz_ssm_import(dz_ctx* ctx, int layer, int seq, const float* state, const float* conv_history,
                         int32_t conv_head);
+/* Synthetic-workload helper (benchmarks, tests): sets the first len rows of K
+ * and V of one (layer, sequence) to a repeated byte pattern and sets the
+ * cache length to len, without a host round trip. */
+dz_status dz_kv_fill_pattern(dz_ctx* ctx, int layer, int seq, int64_t len, int byte_value);
 /* The device RoPE table rows [pos0, pos0+n): cos[64] | sin[64] per row (host out). */
 dz_status dz_rope_table(dz_ctx* ctx, int64_t pos0, int64_t n, float* out);
 
