@@ -80,27 +80,45 @@ def gdn_bytes(B):
 
 
 class Clocks:
-    """Samples nvidia-smi during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """Samples nvidia-smi (clocks and throttle reasons) around the timed region.
 
-    def __init__(self, gpu_id):
+    Sampling starts before the timed region and stops after it; samples whose
+    timestamp falls inside [start, end] are reported.  When the timed region is
+    shorter than the sampling interval, the nearest samples on either side are
+    reported instead and "window" says so."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id, period_ms=50):
         self.gpu_id = gpu_id          # nvidia-smi id (UUID), independent of CUDA_VISIBLE_DEVICES
+        self.period_ms = period_ms
         self.proc = None
         self.raw = ""
+        self.t0 = self.t1 = None
 
     def start(self):
+        import datetime
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", str(self.period_ms)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(1.0)           # let the sampler produce its first rows
         except (FileNotFoundError, OSError):
             self.proc = None
+        self._now = datetime.datetime.now
+
+    def mark_start(self):
+        self.t0 = self._now() if self.proc else None
+
+    def mark_end(self):
+        self.t1 = self._now() if self.proc else None
 
     def stop(self):
+        import datetime
         if self.proc is None:
             return None
+        time.sleep(0.3)
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
@@ -108,23 +126,30 @@ class Clocks:
             self.proc.kill()
             out, _ = self.proc.communicate()
         self.raw = out
-        sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         for line in out.strip().splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f")
+                rows.append((ts, float(f[2]), float(f[3]), [n for n, v in zip(names, f[6:10])
+                                                          if v.lower().startswith("active")]))
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
+        if not rows or self.t0 is None:
             return None
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        inside = [r for r in rows if self.t0 <= r[0] <= self.t1]
+        window = "timed region"
+        if not inside:
+            before = [r for r in rows if r[0] < self.t0][-1:]
+            after = [r for r in rows if r[0] > self.t1][:1]
+            inside = before + after
+            window = "nearest samples around a timed region shorter than the sampling period"
+        reasons = sorted({n for r in inside for n in r[3]})
+        return {"sm_mhz": float(np.median([r[1] for r in inside])), "sm_max_mhz": inside[0][2],
+                "reasons": reasons, "samples": len(inside), "window": window}
 
 
 # ---------------------------------------------------------------------------
@@ -268,6 +293,7 @@ def run_ours(args):
     uuid = str(torch.cuda.get_device_properties(dev).uuid)
     clocks = Clocks(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
     clocks.start()
+    clocks.mark_start()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     launches = 0
@@ -284,6 +310,7 @@ def run_ours(args):
         ev[i][2].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
+    clocks.mark_end()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -571,7 +598,7 @@ def run_stack(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
