@@ -12,15 +12,17 @@
 //   2. pf_prior     : (only when the cache already held tokens) bf16 copies of the
 //                     prior K/V rows for the attention kernel.
 //   3. pf_attn      : one CTA per (q head, 128-token query tile), heaviest tiles
-//                     first.  Warp 4 issues TMA loads (Q once; K and V blocks of 64
-//                     keys into separate 2-stage rings, 128B-swizzled), warp 5 issues
-//                     tcgen05.mma from a single thread: S = Q K^T (M128 N64 K256,
-//                     both operands K-major in SMEM) into one of two TMEM S buffers,
-//                     and O += P V (M128 N256 K64, P from TMEM, V MN-major in SMEM)
-//                     into a 256-column TMEM accumulator.  Warps 0-3 (one TMEM lane
-//                     per query row) run the causal online softmax in log2 units
+//                     first.  Warp 8 issues TMA loads (Q once; K blocks of 128 keys
+//                     as 16 KB 64-dim boxes through a 5-slot ring, V as 16 KB
+//                     32-key slots through a 4-slot ring, all 128B-swizzled), warp 9
+//                     issues tcgen05.mma from a single thread: S = Q K^T (M128 N128
+//                     K256, both operands K-major in SMEM) into one of two TMEM S
+//                     buffers, and O += P V (M128 N256 K128, P from TMEM, V MN-major
+//                     in SMEM) into a 256-column TMEM accumulator.  Warps 0-7 (one
+//                     TMEM lane per query row, two warps per lane quarter splitting
+//                     the 128 keys of a block) run the causal online softmax in log2 units
 //                     with a lazy rescale of O (only when the row max grows by more
-//                     than 2^8), write P as bf16 into TMEM, and finish with
+//                     than 2^8), write P as bf16 over its S columns in TMEM, and finish with
 //                     O / l * sigmoid(gate).
 // All mbarrier waits are bounded (device error word on expiry).
 #include <cuda.h>
@@ -35,22 +37,25 @@ namespace dz {
 namespace pf {
 
 constexpr int BM = 128;        // query rows per CTA
-constexpr int BN = 64;         // keys per block
-constexpr int NTHREADS = 192;  // warps 0-3 softmax, warp 4 TMA, warp 5 MMA
-// TMEM columns: S buffers [0,64) and [64,128) (f32), P buffers [128,160) and
-// [160,192) (bf16 pairs), O accumulator [256,512) (f32)
-__host__ __device__ constexpr uint32_t S_COL(int st) { return 64u * (uint32_t)st; }
-__host__ __device__ constexpr uint32_t P_COL(int st) { return 128u + 32u * (uint32_t)st; }
+constexpr int BN = 128;        // keys per block (S = Q K^T runs as M128 x N128 products)
+constexpr int NK = 5;          // K ring: slots of one 64-dim box of a key block (128 x 64 bf16, 16 KB)
+constexpr int NV = 4;          // V ring: slots of 32 keys x 256 dims (4 boxes of 32 x 64 bf16, 16 KB)
+constexpr int NTHREADS = 320;  // warps 0-7 softmax, warp 8 TMA, warp 9 MMA
+// TMEM columns: S buffers [0,128) and [128,256) (f32); P of a block (bf16 pairs)
+// overwrites the first 64 columns of its own S buffer; O accumulator [256,512)
+__host__ __device__ constexpr uint32_t S_COL(int st) { return 128u * (uint32_t)st; }
 constexpr uint32_t O_COL = 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;   // log2 units
 
 struct alignas(1024) Smem {
     __nv_bfloat16 q[4][BM][64];          // 4 boxes of 64 dims, 16 KB each
-    __nv_bfloat16 k[2][4][BN][64];       // 2 stages x 4 boxes x 8 KB
-    __nv_bfloat16 v[2][4][BN][64];
+    __nv_bfloat16 k[NK][BN][64];         // K ring
+    __nv_bfloat16 v[NV][4][32][64];      // V ring
     uint64_t q_full;
-    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t k_full[NK], k_empty[NK], v_full[NV], v_empty[NV];
     uint64_t s_full[2], p_full[2], pv_done[2];
+    float red_max[2][2][BM];             // [block parity][column half][row] partial row maxima
+    float red_l[2][BM];                  // [column half][row] partial row sums
     uint32_t tmem_base;
 };
 static_assert(offsetof(Smem, k) % 1024 == 0 && offsetof(Smem, v) % 1024 == 0, "swizzle atoms need 1 KB alignment");
@@ -115,6 +120,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
           "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// barrier among a subset of the CTA's warps (id 0 is __syncthreads)
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -291,13 +308,17 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
     }
     if (tid == 0) {
         mbar_init(&sm.q_full, 1);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NK; ++i) {
             mbar_init(&sm.k_full[i], 1);
             mbar_init(&sm.k_empty[i], 1);
+        }
+        for (int i = 0; i < NV; ++i) {
             mbar_init(&sm.v_full[i], 1);
             mbar_init(&sm.v_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.s_full[i], 1);
-            mbar_init(&sm.p_full[i], BM);
+            mbar_init(&sm.p_full[i], 2 * BM);
             mbar_init(&sm.pv_done[i], 1);
         }
         fence_mbar_init();
@@ -308,41 +329,50 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
     const uint32_t tmem = sm.tmem_base;
     bool ok = true;
 
-    if (warp == 4) {
-        // ---------------- TMA producer ----------------
+    if (warp == 8) {
+        // ---------------- TMA producers: lane 0 = Q and K boxes, lane 1 = V slots ----------------
         if (lane == 0) {
             mbar_arrive_expect_tx(&sm.q_full, BM * HD * 2);
             for (int b = 0; b < 4; ++b) tma_load_3d(&sm.q[b][0][0], &tm_q, 64 * b, (int)q0, qh, &sm.q_full);
-            for (int j = 0; j < nblk && ok; ++j) {
-                const int st = j & 1;
-                if (j >= 2 && !wait_or_flag(&sm.k_empty[st], ((j - 2) >> 1) & 1, err, ok)) break;
-                mbar_arrive_expect_tx(&sm.k_full[st], BN * HD * 2);
-                for (int b = 0; b < 4; ++b) tma_load_3d(&sm.k[st][b][0][0], &tm_k, 64 * b, j * BN, kvh, &sm.k_full[st]);
-                if (j >= 2 && !wait_or_flag(&sm.v_empty[st], ((j - 2) >> 1) & 1, err, ok)) break;
-                mbar_arrive_expect_tx(&sm.v_full[st], BN * HD * 2);
-                for (int b = 0; b < 4; ++b) tma_load_3d(&sm.v[st][b][0][0], &tm_v, 64 * b, j * BN, kvh, &sm.v_full[st]);
+            for (int idx = 0; idx < 4 * nblk && ok; ++idx) {
+                const int slot = idx % NK, j = idx >> 2, b = idx & 3;
+                if (idx >= NK && !wait_or_flag(&sm.k_empty[slot], ((idx / NK) - 1) & 1, err, ok)) break;
+                mbar_arrive_expect_tx(&sm.k_full[slot], BN * 64 * 2);
+                tma_load_3d(&sm.k[slot][0][0], &tm_k, 64 * b, j * BN, kvh, &sm.k_full[slot]);
+            }
+        } else if (lane == 1) {
+            for (int idx = 0; idx < 4 * nblk && ok; ++idx) {
+                const int slot = idx % NV, j = idx >> 2, kg = idx & 3;
+                if (idx >= NV && !wait_or_flag(&sm.v_empty[slot], ((idx / NV) - 1) & 1, err, ok)) break;
+                mbar_arrive_expect_tx(&sm.v_full[slot], 32 * HD * 2);
+                for (int d = 0; d < 4; ++d)
+                    tma_load_3d(&sm.v[slot][d][0][0], &tm_v, 64 * d, j * BN + 32 * kg, kvh, &sm.v_full[slot]);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ---------------- MMA issuer (one thread) ----------------
         if (lane == 0) {
             constexpr uint32_t ID_QK = idesc_bf16(BM, BN, false);
             constexpr uint32_t ID_PV = idesc_bf16(BM, HD, true);
             const uint32_t q_s = smem_u32(&sm.q[0][0][0]);
+            const uint32_t k_s = smem_u32(&sm.k[0][0][0]);
+            const uint32_t v_s = smem_u32(&sm.v[0][0][0][0]);
             auto issue_s = [&](int j) {
                 const int st = j & 1;
-                if (!wait_or_flag(&sm.k_full[st], (j >> 1) & 1, err, ok)) return;
-                fence_after_sync();
-                const uint32_t k_s = smem_u32(&sm.k[st][0][0][0]);
+                for (int b = 0; b < 4; ++b) {
+                    const int idx = 4 * j + b, slot = idx % NK;
+                    if (!wait_or_flag(&sm.k_full[slot], (idx / NK) & 1, err, ok)) return;
+                    fence_after_sync();
 #pragma unroll
-                for (int s = 0; s < HD / 16; ++s) {
-                    const uint32_t off_q = (uint32_t)(s >> 2) * (BM * 128) + (uint32_t)(s & 3) * 32;
-                    const uint32_t off_k = (uint32_t)(s >> 2) * (BN * 128) + (uint32_t)(s & 3) * 32;
-                    umma_ss(tmem + S_COL(st), sw128_desc(q_s + off_q, 16, 1024), sw128_desc(k_s + off_k, 16, 1024),
-                            ID_QK, s > 0 ? 1u : 0u);
+                    for (int s4 = 0; s4 < 4; ++s4) {
+                        const uint32_t off_q = (uint32_t)b * (BM * 128) + (uint32_t)s4 * 32;
+                        const uint32_t off_k = (uint32_t)slot * (BN * 128) + (uint32_t)s4 * 32;
+                        umma_ss(tmem + S_COL(st), sw128_desc(q_s + off_q, 16, 1024),
+                                sw128_desc(k_s + off_k, 16, 1024), ID_QK, (b > 0 || s4 > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&sm.k_empty[slot]);
                 }
                 umma_commit(&sm.s_full[st]);
-                umma_commit(&sm.k_empty[st]);
             };
             if (wait_or_flag(&sm.q_full, 0, err, ok)) {
                 issue_s(0);
@@ -350,47 +380,54 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
                 for (int j = 0; j < nblk && ok; ++j) {
                     const int st = j & 1;
                     if (!wait_or_flag(&sm.p_full[st], (j >> 1) & 1, err, ok)) break;
-                    if (!wait_or_flag(&sm.v_full[st], (j >> 1) & 1, err, ok)) break;
-                    fence_after_sync();
-                    const uint32_t v_s = smem_u32(&sm.v[st][0][0][0]);
+                    for (int kg = 0; kg < 4 && ok; ++kg) {
+                        const int idx = 4 * j + kg, slot = idx % NV;
+                        if (!wait_or_flag(&sm.v_full[slot], (idx / NV) & 1, err, ok)) break;
+                        fence_after_sync();
 #pragma unroll
-                    for (int s = 0; s < BN / 16; ++s) {
-                        // B = V[16 keys][256 dims], MN-major: 64-dim boxes 8 KB apart (LBO),
-                        // 8-key swizzle atoms 1 KB apart (SBO)
-                        umma_ts(tmem + O_COL, tmem + P_COL(st) + 8 * s,
-                                sw128_desc(v_s + (uint32_t)s * 16 * 128, BN * 128, 1024), ID_PV,
-                                (j > 0 || s > 0) ? 1u : 0u);
+                        for (int s2 = 0; s2 < 2; ++s2) {
+                            // B = V[16 keys][256 dims], MN-major: 64-dim boxes 4 KB apart (LBO),
+                            // 8-key swizzle atoms 1 KB apart (SBO); A = P columns of those keys
+                            umma_ts(tmem + O_COL, tmem + S_COL(st) + 8 * (2 * kg + s2),
+                                    sw128_desc(v_s + (uint32_t)slot * (32 * HD * 2) + (uint32_t)s2 * 16 * 128,
+                                               32 * 128, 1024),
+                                    ID_PV, (j > 0 || kg > 0 || s2 > 0) ? 1u : 0u);
+                        }
+                        umma_commit(&sm.v_empty[slot]);
                     }
-                    umma_commit(&sm.v_empty[st]);
                     umma_commit(&sm.pv_done[st]);
                     if (j + 2 < nblk) issue_s(j + 2);
                 }
             }
         }
     } else {
-        // ---------------- softmax warpgroup: thread = query row ----------------
-        const int r = tid;                                  // 0..127 = TMEM lane
-        const uint32_t lane_off = (uint32_t)(32 * warp) << 16;
+        // ---------------- softmax: 8 warps, thread = (query row, key half) ----------------
+        const int r = 32 * (warp & 3) + lane;               // TMEM lane = query row
+        const int hf = warp >> 2;                           // keys [64 hf, 64 hf + 64) of a block
+        const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
         const int64_t qpos = base + q0 + r;                 // absolute position of this query row
-        float m_run = -INFINITY, l_run = 0.0f;
+        float m_run = -INFINITY, l_run = 0.0f;              // m identical in both halves; l partial per half
         for (int j = 0; j < nblk; ++j) {
             const int st = j & 1;
             if (!wait_or_flag(&sm.s_full[st], (j >> 1) & 1, err, ok)) break;
             fence_after_sync();
-            float s[BN];
-            tmem_ld32(tmem + lane_off + S_COL(st), s);
-            tmem_ld32(tmem + lane_off + S_COL(st) + 32, s + 32);
-            const int64_t k0 = (int64_t)j * BN;
+            float s[64];
+            tmem_ld32(tmem + lane_off + S_COL(st) + 64 * hf, s);
+            tmem_ld32(tmem + lane_off + S_COL(st) + 64 * hf + 32, s + 32);
+            const int64_t k0 = (int64_t)j * BN + 64 * hf;
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
+            for (int c = 0; c < 64; ++c) {
                 const float x = (k0 + c <= qpos) ? s[c] * LOG2E : -INFINITY;
                 s[c] = x;
                 mx = fmaxf(mx, x);
             }
+            sm.red_max[st][hf][r] = mx;
+            named_bar_sync(1, 256);                          // also: every S read of this block is done
+            mx = fmaxf(mx, sm.red_max[st][hf ^ 1][r]);
             const float m_new = fmaxf(m_run, mx);
             if (m_new > m_run + RESCALE_THRESHOLD) {
-                // lazy rescale: the running max moved a lot -- scale l and this row of O
+                // lazy rescale: the running max moved a lot -- scale l and this half-row of O
                 const float f = ex2(m_run - m_new);
                 l_run *= f;
                 if (j > 0) {
@@ -398,7 +435,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
                     if (!wait_or_flag(&sm.pv_done[pj], ((j - 1) >> 1) & 1, err, ok)) break;
                     fence_after_sync();
 #pragma unroll 1
-                    for (int c = 0; c < HD; c += 32) {
+                    for (int c = 128 * hf; c < 128 * hf + 128; c += 32) {
                         float o[32];
                         uint32_t ob[32];
                         tmem_ld32(tmem + lane_off + O_COL + c, o);
@@ -410,31 +447,33 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
                 m_run = m_new;
             }
             float psum = 0.0f;
-            uint32_t pk[BN / 2];
+            uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < BN; c += 2) {
+            for (int c = 0; c < 64; c += 2) {
                 const float p0 = ex2(s[c] - m_run);
                 const float p1 = ex2(s[c + 1] - m_run);
                 psum += p0 + p1;
                 pk[c / 2] = pack_bf16(p0, p1);
             }
             l_run += psum;
-            // P buffer `st` was last read by PV(j-2)
-            if (j >= 2 && !wait_or_flag(&sm.pv_done[st], ((j - 2) >> 1) & 1, err, ok)) break;
-            fence_after_sync();
-            tmem_st32(tmem + lane_off + P_COL(st), pk);
+            // P of this block goes over the first 64 columns of its own S buffer (the
+            // previous reader of these columns, PV(j-2), completed before S(j) did)
+            tmem_st32(tmem + lane_off + S_COL(st) + 32 * hf, pk);
             fence_before_sync();
             mbar_arrive(&sm.p_full[st]);
         }
-        // epilogue: O / l * sigmoid(gate)
+        // epilogue: O / l * sigmoid(gate); this thread covers dims [128 hf, 128 hf + 128)
+        sm.red_l[hf][r] = l_run;
+        named_bar_sync(1, 256);
+        const float l_tot = l_run + sm.red_l[hf ^ 1][r];
         if (ok) {
             const int jl = nblk - 1;
             if (wait_or_flag(&sm.pv_done[jl & 1], (jl >> 1) & 1, err, ok)) {
                 fence_after_sync();
                 const int64_t t = q0 + r;
-                const float inv_l = 1.0f / l_run;
+                const float inv_l = 1.0f / l_tot;
 #pragma unroll 1
-                for (int c = 0; c < HD; c += 32) {
+                for (int c = 128 * hf; c < 128 * hf + 128; c += 32) {
                     float o[32];
                     tmem_ld32(tmem + lane_off + O_COL + c, o);
                     if (t < T) {
@@ -525,7 +564,7 @@ cudaError_t launch_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
         *n_launch += 1;
     }
     CUtensorMap mq, mk, mv;
-    if (!make_map(&mq, qb, T, nq, pf::BM) || !make_map(&mk, kb, L, kvc, pf::BN) || !make_map(&mv, vb, L, kvc, pf::BN))
+    if (!make_map(&mq, qb, T, nq, pf::BM) || !make_map(&mk, kb, L, kvc, pf::BN) || !make_map(&mv, vb, L, kvc, 32))
         return cudaErrorInvalidValue;
     const int n_qt = (int)((T + pf::BM - 1) / pf::BM);
     const int sc = ctx->cfg.qtile_split_count, si = ctx->cfg.qtile_split_index;
