@@ -158,6 +158,15 @@ cudaError_t ensure_prefill_scratch(dz_ctx* ctx, size_t bytes) {
     if (e == cudaSuccess) ctx->pf_bytes = bytes;
     return e;
 }
+cudaError_t ensure_decode_records(dz_ctx* ctx, size_t bytes) {
+    if (ctx->gdn_rec_bytes >= bytes) return cudaSuccess;
+    if (ctx->gdn_rec) cudaFree(ctx->gdn_rec);
+    ctx->gdn_rec = nullptr;
+    ctx->gdn_rec_bytes = 0;
+    cudaError_t e = cudaMalloc(&ctx->gdn_rec, bytes);
+    if (e == cudaSuccess) ctx->gdn_rec_bytes = bytes;
+    return e;
+}
 }  // namespace dz
 
 extern "C" {
@@ -226,6 +235,7 @@ dz_status dz_ctx_destroy(dz_ctx* ctx) {
                 if (p) cudaFree(p);
         if (ctx->stage) cudaFree(ctx->stage);
         if (ctx->pf) cudaFree(ctx->pf);
+        if (ctx->gdn_rec) cudaFree(ctx->gdn_rec);
         if (ctx->d_err) cudaFree(ctx->d_err);
     }
     delete ctx;

@@ -79,6 +79,9 @@ struct dz_ctx {
     // prefill scratch (grown on demand)
     void* pf = nullptr;
     size_t pf_bytes = 0;
+    // Gated DeltaNet decode records (grown on demand)
+    float* gdn_rec = nullptr;
+    size_t gdn_rec_bytes = 0;
 };
 
 namespace dz {
@@ -95,4 +98,6 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
                                const float* beta, const float* z, float* y, cudaStream_t st, int* n_launch);
 // grows ctx->pf to at least `bytes`
 cudaError_t ensure_prefill_scratch(dz_ctx* ctx, size_t bytes);
+// grows ctx->gdn_rec to at least `bytes`
+cudaError_t ensure_decode_records(dz_ctx* ctx, size_t bytes);
 }  // namespace dz

@@ -1,17 +1,16 @@
-// gdn_decode.cu -- fused Gated DeltaNet decode step.
+// gdn_decode.cu -- Gated DeltaNet decode step.
 //
 // Reference: Daiza-engine/src/model/ssm.rs:466-611 (ssm_forward_into after the
-// projection GEMV).  One CTA per (sequence, v head), 128 threads:
-//   - the head's 64 KB state tile is brought into shared memory by four 16 KB
-//     bulk async copies (one mbarrier per 32-row quarter) that overlap with
-//   - the ring conv1d (k=4) + SiLU of the q/k channels of k head vh % 16 and
-//     the v channels of vh, L2-norm of q and k, q *= 1/sqrt(128), the gates
-//     decay = exp(ssm_a * softplus(alpha + dt_bias)) and beta = sigmoid(b);
-//   - each warp then runs the reference's fused row pass (ssm.rs:378-418) on
-//     its 32 rows straight out of shared memory (decay, kv = S k, delta,
-//     rank-1 update, y = S q; warp-shuffle dot products) and writes its rows
-//     back with one 16 KB bulk store;
-//   - the gated RMSNorm output y * inv_rms * w * silu(z) (ssm.rs:576-611).
+// projection GEMV).  Two stream-ordered kernels:
+//   1. gdn_dec_prep  (CTA per sequence x 8 channel groups): ring conv1d + SiLU,
+//      L2 norms, q scale -> normalised q/k per k head and v per v head; silu(z)
+//      and gates; the ring slot `head` receives the raw input row.
+//   2. gdn_dec_state (persistent, 3 CTAs per SM, launched as a programmatic
+//      dependent of 1): brings each head's 64 KB [128 v][128 k] state tile and
+//      its q/k/record rows in with bulk async copies, runs the reference's fused
+//      row pass out of shared memory (decay, kv = S k, delta, rank-1 update,
+//      y = S q), writes the rows back from registers, then the gated RMSNorm
+//      output.
 // State traffic is exactly one read and one write of each tile.
 #include <cstddef>
 
@@ -19,157 +18,271 @@
 
 namespace dz {
 
-struct GdnSmem {
-    float S[SSM_D][SSM_D];   // 64 KB state tile
-    float q[SSM_D], k[SSM_D], v[SSM_D], y[SSM_D];
-    float red[3][4];
-    float gate[2];           // decay, beta
-    uint64_t bar[4];
-};
-static_assert(offsetof(GdnSmem, q) % 16 == 0 && offsetof(GdnSmem, k) % 16 == 0, "float4-read fields aligned");
+// gdn_dec_prep writes, per sequence b:
+//   qk  [b][32][128]  normalised q (rows 0..15, * 1/sqrt(128)) and k (rows 16..31) of every k head
+//   rec [b*vc + vl][264] = v (conv + SiLU) | silu(z) | decay, beta (+6 pad)
+constexpr int REC_F = 2 * SSM_D + 8;   // 264 floats (1056 B, 16-byte multiple)
+constexpr int PREP_GROUPS = 8;         // 128-channel groups per prep CTA (one per warp)
 
-__device__ __forceinline__ float block_sum128(float x, float* red4) {
-    x = warp_sum(x);
+// ---------------------------------------------------------------------------
+// 1. prep: grid (B, chunks of 8 channel groups + 1).  Groups 0..15 are the q
+//    channels of k head g, 16..31 the k channels, 32.. the v channels of the
+//    local v heads: ring conv1d + SiLU (the reference's tap and FMA order,
+//    ssm.rs:492-513), L2 norms (eps on the sum), q scale; the ring slot `head`
+//    (the oldest, read by nobody this step) receives the raw row.  The last
+//    chunk computes silu(z) and the gates decay = exp(ssm_a * softplus(alpha +
+//    dt_bias)), beta = sigmoid(b).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) gdn_dec_prep_kernel(GdnDecodeDesc d, int vh0, int vc,
+                                                           const SsmSlot* __restrict__ ssm,
+                                                           const float* __restrict__ conv_w,
+                                                           const float* __restrict__ ssm_a,
+                                                           const float* __restrict__ dt_bias,
+                                                           const float* __restrict__ qkv,
+                                                           const float* __restrict__ alpha_in,
+                                                           const float* __restrict__ beta_in,
+                                                           const float* __restrict__ z_in, float* __restrict__ qk,
+                                                           float* __restrict__ rec) {
+    // the state kernel may start its tile copies now; it waits for this grid's
+    // writes before reading q/k/records
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int b = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) red4[warp] = x;
-    __syncthreads();
-    return red4[0] + red4[1] + red4[2] + red4[3];
+    const int n_groups = 2 * SSM_HK + vc;
+    const int n_chunks = (n_groups + PREP_GROUPS - 1) / PREP_GROUPS;
+    if ((int)blockIdx.y == n_chunks) {
+        // silu(z) and gates for every local v head
+        for (int vl = warp; vl < vc; vl += 8) {
+            const int vh = vh0 + vl;
+            float* r = rec + ((size_t)b * vc + vl) * REC_F;
+            const float4 zz = *reinterpret_cast<const float4*>(z_in + (size_t)b * INNER + (size_t)vh * SSM_D + 4 * lane);
+            *reinterpret_cast<float4*>(r + SSM_D + 4 * lane) =
+                make_float4(siluf_acc(zz.x), siluf_acc(zz.y), siluf_acc(zz.z), siluf_acc(zz.w));
+            if (lane == 0) {
+                const float g = ssm_a[vh] * softplus_ref(alpha_in[(size_t)b * SSM_HV + vh] + dt_bias[vh]);
+                r[2 * SSM_D] = expf(g);
+                r[2 * SSM_D + 1] = sigmoidf_acc(beta_in[(size_t)b * SSM_HV + vh]);
+            }
+        }
+        return;
+    }
+    const int gi = blockIdx.y * PREP_GROUPS + warp;
+    if (gi >= n_groups) return;
+    const SsmSlot slot = ssm[d.sid[b]];
+    float* hist = slot.hist;
+    const int head = d.head[b];
+    const int r0 = (head + 1) & 3, r1 = (head + 2) & 3, r2 = (head + 3) & 3;
+    const float* row_in = qkv + (size_t)b * QKV_LEN;
+    int cb;
+    if (gi < SSM_HK) cb = gi * SSM_D;
+    else if (gi < 2 * SSM_HK) cb = QKD + (gi - SSM_HK) * SSM_D;
+    else cb = 2 * QKD + (vh0 + gi - 2 * SSM_HK) * SSM_D;
+    const int ch = cb + 4 * lane;
+    const float4 h0 = *reinterpret_cast<const float4*>(hist + (size_t)r0 * QKV_LEN + ch);
+    const float4 h1 = *reinterpret_cast<const float4*>(hist + (size_t)r1 * QKV_LEN + ch);
+    const float4 h2 = *reinterpret_cast<const float4*>(hist + (size_t)r2 * QKV_LEN + ch);
+    const float4 cur = *reinterpret_cast<const float4*>(row_in + ch);
+    const float4 w0 = *reinterpret_cast<const float4*>(conv_w + 0 * QKV_LEN + ch);
+    const float4 w1 = *reinterpret_cast<const float4*>(conv_w + 1 * QKV_LEN + ch);
+    const float4 w2 = *reinterpret_cast<const float4*>(conv_w + 2 * QKV_LEN + ch);
+    const float4 w3 = *reinterpret_cast<const float4*>(conv_w + 3 * QKV_LEN + ch);
+    float4 a;
+    a.x = fmaf(cur.x, w3.x, fmaf(h2.x, w2.x, fmaf(h1.x, w1.x, fmaf(h0.x, w0.x, 0.0f))));
+    a.y = fmaf(cur.y, w3.y, fmaf(h2.y, w2.y, fmaf(h1.y, w1.y, fmaf(h0.y, w0.y, 0.0f))));
+    a.z = fmaf(cur.z, w3.z, fmaf(h2.z, w2.z, fmaf(h1.z, w1.z, fmaf(h0.z, w0.z, 0.0f))));
+    a.w = fmaf(cur.w, w3.w, fmaf(h2.w, w2.w, fmaf(h1.w, w1.w, fmaf(h0.w, w0.w, 0.0f))));
+    a = make_float4(siluf_acc(a.x), siluf_acc(a.y), siluf_acc(a.z), siluf_acc(a.w));
+    bool write_ring;
+    if (gi < 2 * SSM_HK) {
+        const float ss = warp_sum(a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w);
+        const float inv = 1.0f / sqrtf(ss + 1e-6f);
+        a = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+        if (gi < SSM_HK) {
+            const float qs = 1.0f / sqrtf((float)SSM_D);
+            a = make_float4(a.x * qs, a.y * qs, a.z * qs, a.w * qs);
+        }
+        *reinterpret_cast<float4*>(qk + ((size_t)b * 2 * SSM_HK + gi) * SSM_D + 4 * lane) = a;
+        const int kh = gi % SSM_HK;
+        // the ring keeps q/k channels of k heads some local v head uses
+        const int first = vh0 + (((kh - vh0) % SSM_HK) + SSM_HK) % SSM_HK;
+        write_ring = first < vh0 + vc;
+    } else {
+        const int vl = gi - 2 * SSM_HK;
+        *reinterpret_cast<float4*>(rec + ((size_t)b * vc + vl) * REC_F + 4 * lane) = a;
+        write_ring = true;
+    }
+    if (write_ring) *reinterpret_cast<float4*>(hist + (size_t)head * QKV_LEN + ch) = cur;
 }
 
-__global__ void __launch_bounds__(128) gdn_decode_kernel(GdnDecodeDesc d, int vh0, const SsmSlot* __restrict__ ssm,
-                                                         const float* __restrict__ conv_w,
-                                                         const float* __restrict__ ssm_a,
-                                                         const float* __restrict__ dt_bias,
-                                                         const float* __restrict__ norm_w,
-                                                         const float* __restrict__ qkv,
-                                                         const float* __restrict__ alpha_in,
-                                                         const float* __restrict__ beta_in,
-                                                         const float* __restrict__ z_in, float* __restrict__ y_out,
-                                                         int vcount, int* err) {
+// ---------------------------------------------------------------------------
+// 2. state pass: persistent CTAs (STATE_CPS per SM, 8 warps each) walk their
+//    items (sequence, v head); per item one bulk copy brings the 64 KB
+//    [128 v][128 k] tile and the q/k/record rows into shared memory.  The row
+//    pass follows the reference's fused update (ssm.rs:390-417): S *= decay,
+//    kv = S k, delta = (v - kv) beta, S += k delta^T, y = S q.  A warp takes 4
+//    rows at a time, 8 lanes per row (16 columns each, three shuffle levels per
+//    dot product), and stores the updated rows straight from registers.  The
+//    next item's copy is issued as soon as the tile is consumed, under the
+//    gated RMSNorm output (ssm.rs:576-611).  The first tile is requested before
+//    the programmatic-dependency wait, so it streams in while gdn_dec_prep is
+//    still finishing.
+// ---------------------------------------------------------------------------
+constexpr int STATE_CPS = 3;   // resident CTAs per SM (3 x 67 KB shared memory)
+struct alignas(128) RecBuf {
+    float q[SSM_D], k[SSM_D];
+    float r[REC_F];            // v | silu(z) | decay, beta
+};
+struct GdnSmem {
+    float S[SSM_D][SSM_D];     // 64 KB
+    RecBuf rec[2];
+    float y[SSM_D];
+    float red[8];
+    uint64_t full;
+};
+static_assert(offsetof(GdnSmem, rec) % 16 == 0 && sizeof(RecBuf) % 16 == 0 && offsetof(RecBuf, k) % 16 == 0 &&
+                  offsetof(RecBuf, r) % 16 == 0,
+              "bulk-copy alignment");
+
+__global__ void __launch_bounds__(256, STATE_CPS) gdn_dec_state_kernel(GdnDecodeDesc d, int vh0, int vc,
+                                                                      const SsmSlot* __restrict__ ssm,
+                                                                      const float* __restrict__ norm_w,
+                                                                      const float* __restrict__ qk,
+                                                                      const float* __restrict__ rec,
+                                                                      float* __restrict__ y_out, int n_items,
+                                                                      int* err) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     GdnSmem& sm = *reinterpret_cast<GdnSmem*>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int vl = blockIdx.x;                 // local v head
-    const int vh = vh0 + vl;                   // global v head
-    const int b = blockIdx.y;
-    const int kh = vh % SSM_HK;                // tiled k-head map (ssm.rs:558-561)
-    const SsmSlot slot = ssm[d.sid[b]];
-    float* Sg = slot.state + (size_t)vl * SSM_D * SSM_D;
-    float* hist = slot.hist;
-    const int head = d.head[b];
-
+    const int g = lane >> 3, c = lane & 7;   // row within a 4-row group, column lane
+    auto state_ptr = [&](int item) {
+        const int b = item / vc, vl = item - b * vc;
+        return ssm[d.sid[b]].state + (size_t)vl * SSM_D * SSM_D;
+    };
+    constexpr uint32_t TILE_BYTES = SSM_D * SSM_D * 4;
+    constexpr uint32_t REC_BYTES = 2 * SSM_D * 4 + REC_F * 4;
+    auto issue_records = [&](int item, int slot) {
+        const int b = item / vc, kh = (vh0 + item - b * vc) % SSM_HK;
+        RecBuf& R = sm.rec[slot];
+        bulk_g2s(&R.q[0], qk + ((size_t)b * 2 * SSM_HK + kh) * SSM_D, SSM_D * 4, &sm.full);
+        bulk_g2s(&R.k[0], qk + ((size_t)b * 2 * SSM_HK + SSM_HK + kh) * SSM_D, SSM_D * 4, &sm.full);
+        bulk_g2s(&R.r[0], rec + (size_t)item * REC_F, REC_F * 4, &sm.full);
+    };
     if (tid == 0) {
-        for (int i = 0; i < 4; ++i) mbar_init(&sm.bar[i], 1);
+        mbar_init(&sm.full, 1);
         fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0) {
-        for (int i = 0; i < 4; ++i) {
-            mbar_arrive_expect_tx(&sm.bar[i], 32 * SSM_D * 4);
-            bulk_g2s(&sm.S[32 * i][0], Sg + (size_t)32 * i * SSM_D, 32 * SSM_D * 4, &sm.bar[i]);
+        if ((int)blockIdx.x < n_items) {
+            mbar_arrive_expect_tx(&sm.full, TILE_BYTES + REC_BYTES);
+            bulk_g2s(&sm.S[0][0], state_ptr(blockIdx.x), TILE_BYTES, &sm.full);
         }
     }
-
-    // ---- conv1d ring + SiLU (ssm.rs:473-518).  Taps t=0..2 are the ring rows
-    // (head+1+t)%4 (oldest first), tap 3 is the current token.
-    const float* row_in = qkv + (size_t)b * QKV_LEN;
-    const int r0 = (head + 1) & 3, r1 = (head + 2) & 3, r2 = (head + 3) & 3;
-    const int chq = kh * SSM_D + tid, chk = QKD + kh * SSM_D + tid, chv = 2 * QKD + vh * SSM_D + tid;
-    float cq, ck, cv;
-    {
-        auto conv = [&](int ch) {
-            float acc = 0.0f;
-            acc = fmaf(hist[(size_t)r0 * QKV_LEN + ch], conv_w[0 * QKV_LEN + ch], acc);
-            acc = fmaf(hist[(size_t)r1 * QKV_LEN + ch], conv_w[1 * QKV_LEN + ch], acc);
-            acc = fmaf(hist[(size_t)r2 * QKV_LEN + ch], conv_w[2 * QKV_LEN + ch], acc);
-            acc = fmaf(row_in[ch], conv_w[3 * QKV_LEN + ch], acc);
-            return siluf_acc(acc);
-        };
-        cq = conv(chq);
-        ck = conv(chk);
-        cv = conv(chv);
-    }
-    // ring write of the current row into slot `head` (the oldest; nobody reads it
-    // this step).  q/k channels of kh are written by the first local v head that
-    // maps to kh; v channels by their own head.
-    if (vh - SSM_HK < vh0) {
-        hist[(size_t)head * QKV_LEN + chq] = row_in[chq];
-        hist[(size_t)head * QKV_LEN + chk] = row_in[chk];
-    }
-    hist[(size_t)head * QKV_LEN + chv] = row_in[chv];
-
-    // ---- L2 norm (eps on the sum, ssm.rs:123) and q scale
-    const float ssq = block_sum128(cq * cq, sm.red[0]);
-    const float ssk = block_sum128(ck * ck, sm.red[1]);
-    const float qs = 1.0f / sqrtf((float)SSM_D);
-    sm.q[tid] = (cq * (1.0f / sqrtf(ssq + 1e-6f))) * qs;
-    sm.k[tid] = ck * (1.0f / sqrtf(ssk + 1e-6f));
-    sm.v[tid] = cv;
-    if (tid == 0) {
-        const float g = ssm_a[vh] * softplus_ref(alpha_in[(size_t)b * SSM_HV + vh] + dt_bias[vh]);
-        sm.gate[0] = expf(g);
-        sm.gate[1] = sigmoidf_acc(beta_in[(size_t)b * SSM_HV + vh]);
-    }
+    // q/k/records come from gdn_dec_prep
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (tid == 0 && (int)blockIdx.x < n_items) issue_records(blockIdx.x, 0);
     __syncthreads();
-
-    // ---- fused row pass on this warp's 32 rows (ssm.rs:390-417)
-    const float decay = sm.gate[0], beta = sm.gate[1];
-    const float4 kq = *reinterpret_cast<const float4*>(&sm.k[4 * lane]);
-    const float4 qq = *reinterpret_cast<const float4*>(&sm.q[4 * lane]);
-    bool ok = mbar_wait(&sm.bar[warp], 0, err);
-    if (ok) {
-#pragma unroll 4
-        for (int r = 0; r < 32; ++r) {
-            const int i = 32 * warp + r;
-            float4 s = *reinterpret_cast<const float4*>(&sm.S[i][4 * lane]);
-            s.x *= decay; s.y *= decay; s.z *= decay; s.w *= decay;
-            float kv = s.x * kq.x;
-            kv = fmaf(s.y, kq.y, kv);
-            kv = fmaf(s.z, kq.z, kv);
-            kv = fmaf(s.w, kq.w, kv);
-            kv = warp_sum(kv);
-            const float di = (sm.v[i] - kv) * beta;
-            s.x = fmaf(di, kq.x, s.x);
-            s.y = fmaf(di, kq.y, s.y);
-            s.z = fmaf(di, kq.z, s.z);
-            s.w = fmaf(di, kq.w, s.w);
-            float yy = s.x * qq.x;
-            yy = fmaf(s.y, qq.y, yy);
-            yy = fmaf(s.z, qq.z, yy);
-            yy = fmaf(s.w, qq.w, yy);
-            yy = warp_sum(yy);
-            *reinterpret_cast<float4*>(&sm.S[i][4 * lane]) = s;
-            if (lane == 0) sm.y[i] = yy;
+    const float nw = norm_w[tid & (SSM_D - 1)];
+    int k = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++k) {
+        if (!mbar_wait(&sm.full, (uint32_t)(k & 1), err)) return;
+        const RecBuf& R = sm.rec[k & 1];
+        float* gS = state_ptr(item);
+        const float decay = R.r[2 * SSM_D], beta = R.r[2 * SSM_D + 1];
+        float4 kq[4], qq[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            kq[j] = *reinterpret_cast<const float4*>(&R.k[32 * j + 4 * c]);
+            qq[j] = *reinterpret_cast<const float4*>(&R.q[32 * j + 4 * c]);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-            bulk_s2g(Sg + (size_t)32 * warp * SSM_D, &sm.S[32 * warp][0], 32 * SSM_D * 4);
-            bulk_commit();
+#pragma unroll 2
+        for (int it = 0; it < 4; ++it) {
+            const int i = 16 * warp + 4 * it + g;
+            float4 sv[4];
+            float kv = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                sv[j] = *reinterpret_cast<const float4*>(&sm.S[i][32 * j + 4 * c]);
+                sv[j].x *= decay; sv[j].y *= decay; sv[j].z *= decay; sv[j].w *= decay;
+                kv = fmaf(sv[j].x, kq[j].x, kv);
+                kv = fmaf(sv[j].y, kq[j].y, kv);
+                kv = fmaf(sv[j].z, kq[j].z, kv);
+                kv = fmaf(sv[j].w, kq[j].w, kv);
+            }
+            kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+            kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+            kv += __shfl_xor_sync(0xffffffffu, kv, 4);
+            const float di = (R.r[i] - kv) * beta;
+            float yy = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                sv[j].x = fmaf(di, kq[j].x, sv[j].x);
+                sv[j].y = fmaf(di, kq[j].y, sv[j].y);
+                sv[j].z = fmaf(di, kq[j].z, sv[j].z);
+                sv[j].w = fmaf(di, kq[j].w, sv[j].w);
+                yy = fmaf(sv[j].x, qq[j].x, yy);
+                yy = fmaf(sv[j].y, qq[j].y, yy);
+                yy = fmaf(sv[j].z, qq[j].z, yy);
+                yy = fmaf(sv[j].w, qq[j].w, yy);
+                // the next read of this state is a whole layer stack away: streaming store
+                __stcs(reinterpret_cast<float4*>(gS + (size_t)i * SSM_D + 32 * j + 4 * c), sv[j]);
+            }
+            yy += __shfl_xor_sync(0xffffffffu, yy, 1);
+            yy += __shfl_xor_sync(0xffffffffu, yy, 2);
+            yy += __shfl_xor_sync(0xffffffffu, yy, 4);
+            if (c == 0) sm.y[i] = yy;
         }
+        __syncthreads();   // tile consumed, y complete
+        const int nxt = item + gridDim.x;
+        if (tid == 0 && nxt < n_items) {
+            mbar_arrive_expect_tx(&sm.full, TILE_BYTES + REC_BYTES);
+            bulk_g2s(&sm.S[0][0], state_ptr(nxt), TILE_BYTES, &sm.full);
+            issue_records(nxt, (k + 1) & 1);
+        }
+        // gated RMSNorm: threads 0..127 own one element of y
+        float yv = 0.0f;
+        if (tid < SSM_D) yv = sm.y[tid];
+        float ss = warp_sum(yv * yv);
+        if (lane == 0) sm.red[warp] = ss;
+        __syncthreads();
+        if (tid < SSM_D) {
+            ss = sm.red[0] + sm.red[1] + sm.red[2] + sm.red[3];
+            const float inv = 1.0f / sqrtf(ss * (1.0f / (float)SSM_D) + 1e-6f);
+            y_out[(size_t)item * SSM_D + tid] = ((yv * inv) * nw) * R.r[SSM_D + tid];
+        }
+        __syncthreads();   // y, red and this record slot are reused two items on
     }
-    __syncthreads();
-
-    // ---- gated RMSNorm output (ssm.rs:576-611): y * inv_rms * w * silu(z)
-    const float yv = sm.y[tid];
-    const float ss = block_sum128(yv * yv, sm.red[2]);
-    const float inv = 1.0f / sqrtf(ss * (1.0f / (float)SSM_D) + 1e-6f);
-    const float zt = z_in[(size_t)b * INNER + (size_t)vh * SSM_D + tid];
-    y_out[((size_t)b * vcount + vl) * SSM_D + tid] = ((yv * inv) * norm_w[tid]) * siluf_acc(zt);
-    if (ok && lane == 0) bulk_wait_all();
 }
 
 cudaError_t launch_gdn_decode(dz_ctx* ctx, int layer, const GdnDecodeDesc& d, const float* qkv,
                               const float* alpha, const float* beta, const float* z, float* y,
                               cudaStream_t st, int* n_launch) {
     const LayerState& L = ctx->layers[layer];
-    const int vc = ctx->cfg.v_head_count;
-    cudaFuncSetAttribute(gdn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(GdnSmem));
-    gdn_decode_kernel<<<dim3(vc, d.B), 128, sizeof(GdnSmem), st>>>(d, ctx->cfg.v_head_begin, L.d_ssm, L.conv_w,
-                                                                   L.ssm_a, L.dt_bias, L.norm_w, qkv, alpha, beta,
-                                                                   z, y, vc, ctx->d_err);
-    *n_launch += 1;
-    return cudaGetLastError();
+    const int vc = ctx->cfg.v_head_count, vh0 = ctx->cfg.v_head_begin;
+    const int items = d.B * vc;
+    const size_t qk_floats = (size_t)d.B * 2 * SSM_HK * SSM_D;
+    cudaError_t e = ensure_decode_records(ctx, (qk_floats + (size_t)items * REC_F) * sizeof(float));
+    if (e != cudaSuccess) return e;
+    float* qk = ctx->gdn_rec;
+    float* rec = qk + qk_floats;
+    const int n_chunks = (2 * SSM_HK + vc + PREP_GROUPS - 1) / PREP_GROUPS;
+    gdn_dec_prep_kernel<<<dim3(d.B, n_chunks + 1), 256, 0, st>>>(d, vh0, vc, L.d_ssm, L.conv_w, L.ssm_a, L.dt_bias,
+                                                                qkv, alpha, beta, z, qk, rec);
+    e = cudaFuncSetAttribute(gdn_dec_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(GdnSmem));
+    if (e != cudaSuccess) return e;
+    // programmatic dependent launch: the state kernel's CTAs start their first
+    // tile copy while the prep grid drains
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(items < ctx->n_sm * STATE_CPS ? items : ctx->n_sm * STATE_CPS);
+    lc.blockDim = dim3(256);
+    lc.dynamicSmemBytes = sizeof(GdnSmem);
+    lc.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&lc, gdn_dec_state_kernel, d, vh0, vc, (const SsmSlot*)L.d_ssm, (const float*)L.norm_w,
+                           (const float*)qk, (const float*)rec, y, items, ctx->d_err);
+    *n_launch += 2;
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace dz
