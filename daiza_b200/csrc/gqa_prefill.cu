@@ -110,6 +110,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 32 columns into registers without waiting (pair with tmem_wait_ld)
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -159,6 +171,32 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// three-input maximum (sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// packed f32x2 arithmetic on register pairs (sm_100)
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t sub_f2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -243,8 +281,10 @@ __global__ void __launch_bounds__(256) pf_prep_kernel(int kvc, int64_t T, int64_
                              fmaf(x0.w, c.w, pr.w * s.w));
         }
         if (task < nq) {
-            x0 = make_float4(x0.x * 0.0625f, x0.y * 0.0625f, x0.z * 0.0625f, x0.w * 0.0625f);
-            x1 = make_float4(x1.x * 0.0625f, x1.y * 0.0625f, x1.z * 0.0625f, x1.w * 0.0625f);
+            // 1/sqrt(256) and log2(e): the attention kernel's scores come out in log2 units
+            constexpr float QS = 0.0625f * 1.4426950408889634f;
+            x0 = make_float4(x0.x * QS, x0.y * QS, x0.z * QS, x0.w * QS);
+            x1 = make_float4(x1.x * QS, x1.y * QS, x1.z * QS, x1.w * QS);
             __nv_bfloat16* qd = qb + ((size_t)task * T + t) * HD;
             st4_bf16(qd + 4 * lane, x0);
             st4_bf16(qd + 128 + 4 * lane, x1);
@@ -412,15 +452,32 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
             if (!wait_or_flag(&sm.s_full[st], (j >> 1) & 1, err, ok)) break;
             fence_after_sync();
             float s[64];
-            tmem_ld32(tmem + lane_off + S_COL(st) + 64 * hf, s);
-            tmem_ld32(tmem + lane_off + S_COL(st) + 64 * hf + 32, s + 32);
-            const int64_t k0 = (int64_t)j * BN + 64 * hf;
-            float mx = -INFINITY;
+            {
+                uint32_t raw[64];
+                tmem_ld32_async(tmem + lane_off + S_COL(st) + 64 * hf, raw);
+                tmem_ld32_async(tmem + lane_off + S_COL(st) + 64 * hf + 32, raw + 32);
+                tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                const float x = (k0 + c <= qpos) ? s[c] * LOG2E : -INFINITY;
-                s[c] = x;
-                mx = fmaxf(mx, x);
+                for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(raw[c]);
+            }
+            // causal mask: keys k0 + c with c > lim are in the future (only blocks on the diagonal)
+            const int64_t lim64 = qpos - ((int64_t)j * BN + 64 * hf);
+            if (lim64 < 63) {
+                const int lim = lim64 < -1 ? -1 : (int)lim64;
+#pragma unroll
+                for (int c = 0; c < 64; ++c) s[c] = c > lim ? -INFINITY : s[c];
+            }
+            float mx;
+            {
+                float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+#pragma unroll
+                for (int c = 4; c < 64; c += 8) {
+                    a0 = max3f(a0, s[c], s[c + 1]);
+                    a1 = max3f(a1, s[c + 2], s[c + 3]);
+                    a2 = max3f(a2, s[c + 4], s[c + 5]);
+                    a3 = max3f(a3, s[c + 6], s[c + 7]);
+                }
+                mx = fmaxf(max3f(a0, a1, a2), a3);
             }
             sm.red_max[st][hf][r] = mx;
             named_bar_sync(1, 256);                          // also: every S read of this block is done
@@ -446,16 +503,25 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
                 }
                 m_run = m_new;
             }
-            float psum = 0.0f;
             uint32_t pk[32];
+            {
+                const uint64_t mm = f2(m_run, m_run);
+                uint64_t acc0 = f2(0.0f, 0.0f), acc1 = acc0;
 #pragma unroll
-            for (int c = 0; c < 64; c += 2) {
-                const float p0 = ex2(s[c] - m_run);
-                const float p1 = ex2(s[c + 1] - m_run);
-                psum += p0 + p1;
-                pk[c / 2] = pack_bf16(p0, p1);
+                for (int c = 0; c < 64; c += 4) {
+                    float x0, x1, x2, x3;
+                    f2_split(sub_f2(f2(s[c], s[c + 1]), mm), x0, x1);
+                    f2_split(sub_f2(f2(s[c + 2], s[c + 3]), mm), x2, x3);
+                    const float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
+                    acc0 = add_f2(acc0, f2(p0, p1));
+                    acc1 = add_f2(acc1, f2(p2, p3));
+                    pk[c / 2] = pack_bf16(p0, p1);
+                    pk[c / 2 + 1] = pack_bf16(p2, p3);
+                }
+                float u0, u1;
+                f2_split(add_f2(acc0, acc1), u0, u1);
+                l_run += u0 + u1;
             }
-            l_run += psum;
             // P of this block goes over the first 64 columns of its own S buffer (the
             // previous reader of these columns, PV(j-2), completed before S(j) did)
             tmem_st32(tmem + lane_off + S_COL(st) + 32 * hf, pk);
