@@ -19,10 +19,17 @@ constexpr float LOG2E = 1.4426950408889634f;
 // code here and return instead of hanging (read by dz_device_error()).
 enum : int { DEVERR_NONE = 0, DEVERR_MBAR_TIMEOUT = 1 };
 
-// Spin limit for mbarrier waits.  A bulk copy of a few tens of KB completes
-// in microseconds; 2^26 polls (each try_wait may itself block for a
-// hardware-defined slice) is seconds, far beyond any legitimate wait.
-constexpr uint32_t MBAR_SPIN_LIMIT = 1u << 26;
+// Time limit for an mbarrier wait, read from the %globaltimer nanosecond clock.
+// Every legitimate wait in these kernels (a bulk copy, a tensor-core product,
+// another warp's epilogue) ends within microseconds; one second means the
+// phase will never complete.
+constexpr uint64_t MBAR_WAIT_LIMIT_NS = 1000000000ull;
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -52,10 +59,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait.  Returns false (and records DEVERR_MBAR_TIMEOUT) if the phase
-// did not complete within MBAR_SPIN_LIMIT polls.
+// did not complete within MBAR_WAIT_LIMIT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-    for (uint32_t i = 0; i < MBAR_SPIN_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0 && global_ns() - t0 > MBAR_WAIT_LIMIT_NS) break;
+    }
     if (err) atomicExch(err, DEVERR_MBAR_TIMEOUT);
     return false;
 }

@@ -1,4 +1,4 @@
-// gdn_prefill.cu -- chunked (C = 64) Gated DeltaNet prefill.
+// gdn_prefill.cu -- chunked (C = 64) Gated DeltaNet prefill on the tcgen05 tensor cores.
 //
 // Reference: Daiza-engine/src/model/forward.rs:897-1059 -- Phase A (conv1d from
 // in-batch rows or pre-batch ring slots (h0+t+ct+1)%4, SiLU, L2-norm q/k,
@@ -8,101 +8,121 @@
 //
 // The token recurrence  S_t = e^{g_t} S_{t-1} + u_t k_t^T,
 //                        u_t = beta_t (v_t - e^{g_t} S_{t-1} k_t),  y_t = S_t q_t
-// is evaluated chunk by chunk (WY / UT form).  With G the in-chunk cumulative
-// log decay, Gam_ts = e^{G_t - G_s}, A = strict_lower(beta_t Gam_ts k_t.k_s) and
-// Tm = (I + A)^-1:
-//   U0 = Tm diag(beta) V,   W = Tm diag(beta e^G) K                (intra, parallel)
-//   U  = U0 - W S0^T
-//   Y  = diag(e^G) Q S0^T + (lower_incl(Gam) o Q K^T) U
-//   S_C = e^{G_last} S0 + U^T diag(e^{G_last - G}) K                 (inter, sequential)
-// All exponents are <= 0 (no overflow).  Kernels:
-//   gdn_pf_conv   per token: conv + SiLU + L2 norms + gates (log decay, beta)
+// (S stored [v][k]) is evaluated chunk by chunk in WY / UT form.  With G the
+// in-chunk cumulative log decay, Gam_ts = e^{G_t - G_s},
+// A = strict_lower(beta_t Gam_ts k_t.k_s) and Tm = (I + A)^-1:
+//   U0 = Tm diag(beta) V,   W = Tm diag(beta e^G) K                  (per chunk)
+//   U  = U0 - W S^T
+//   Y  = diag(e^G) Q S^T + (lower_incl(Gam) o Q K^T) U
+//   S' = e^{G_last} S + U^T diag(e^{G_last - G}) K                    (chunk to chunk)
+// Every exponent is <= 0.
+//
+// Every matrix product runs on tcgen05 (kind::f16, f32 accumulation in TMEM)
+// with both operands split into bf16 hi + lo halves and three products
+// hi*hi + hi*lo + lo*hi, which keeps ~16 mantissa bits: the outputs and the
+// final state stay ~1e-5 (relative, max-norm) from the f32 token recurrence.
+//
+// Kernels (stream-ordered):
+//   gdn_pf_prep   per token: conv + SiLU + L2 norms + q scale + gates; writes
+//                 q, k (every k head) and v (local v heads) as bf16 hi/lo rows
+//                 [head][hi|lo][Tp][128] for TMA, log decay g and beta [head][Tp]
 //   gdn_pf_ring   ring-buffer update (after every conv read)
-//   gdn_pf_intra  per (chunk, v head): G, K K^T, Q K^T, Tm by forward
-//                 substitution, W, U0, Q e^G, K e^{G_last-G}
-//   gdn_pf_inter  per (v head, 32-row block of S): the chunk recurrence
-//   gdn_pf_gate   per token: y * inv_rms * w * silu(z)
+//   gdn_pf_intra  one CTA per (chunk, v head): [K;Q] K^T, A and P, Tm by
+//                 blocked forward substitution, W^T = K^T (Tm diag(beta e^G))^T
+//                 and U0^T = V^T (Tm diag(beta))^T; writes an 80 KB record
+//                 (W and P as ready-to-use operand images, U0^T, G)
+//   gdn_pf_chain  one persistent CTA per v head: the state lives in TMEM as
+//                 the f32 accumulator [128 v lanes][128 k columns] for the whole
+//                 prefill; per chunk  U^T = U0^T - S W^T,  Y^T = S Qe^T + U^T P^T,
+//                 S = e^{G_last} S + U^T Kd, with warp-specialised loader, MMA
+//                 issuer and epilogues; the gated RMSNorm output is fused.
 #include <cstddef>
 
 #include "dz_internal.h"
+#include "tc_common.cuh"
 
 namespace dz {
 
 namespace gp {
 constexpr int C = 64;            // chunk length
 constexpr int D = SSM_D;         // 128
-constexpr int KP = D + 4;        // padded smem row (floats) for 128-wide rows
-constexpr int MP = C + 1;        // padded smem row for 64x64 matrices
-constexpr int VB = 16;           // state rows per inter CTA
-// Row strides that make warp-level tensor-core fragment reads bank-conflict
-// free: A / transposed-B fragments want a stride == 4 (mod 32) floats,
-// row-major B fragments a stride == 8 (mod 32).
-constexpr int SA = D + 4;    // 132
-constexpr int SB = D + 8;    // 136
-constexpr int SP = C + 4;    // 68
-// per (chunk, v head) record, rows already at the padded strides so that the
-// inter kernel moves each operand with ONE bulk copy:
-//   X [128][SA] (rows 0..63 = W, 64..127 = Q e^G), U0 [D/VB v-blocks][64][VB],
-//   Kd [64][SB], P [64][SP], e^{G_last} (+3 pad)
-constexpr size_t OFF_X = 0, OFF_U0 = OFF_X + 2 * C * SA, OFF_KD = OFF_U0 + C * D, OFF_P = OFF_KD + C * SB,
-                 OFF_EG = OFF_P + C * SP, REC = OFF_EG + 4;
-static_assert(REC % 4 == 0 && OFF_U0 % 4 == 0 && OFF_KD % 4 == 0 && OFF_P % 4 == 0, "16-byte aligned fields");
+// one (chunk, local v head) record written by gdn_pf_intra, read by gdn_pf_chain
+constexpr uint32_t REC_W = 0;          // W  bf16 [hi|lo][k-box 2][64 t][64 k], K-major SW128 images (32 KB)
+constexpr uint32_t REC_U0 = 32768;     // U0^T f32 [t-box 2][128 v][32 t], 16-byte chunks XOR-swizzled by v (32 KB)
+constexpr uint32_t REC_P = 65536;      // P  bf16 [hi|lo][64 t][64 s], K-major SW128 images (16 KB)
+constexpr uint32_t REC_G = 81920;      // G  f32 [64] in-chunk cumulative log decay
+constexpr uint32_t REC_BYTES = 81920 + 256;
 }  // namespace gp
 
 // ---------------------------------------------------------------------------
-// Phase A: conv1d + SiLU + L2 norms + gates, one CTA per token
+// Phase A: conv1d + SiLU + L2 norms + gates, one CTA per (padded) token
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) gdn_pf_conv_kernel(int64_t T, int vh0, int vc, int h0,
+__device__ __forceinline__ void store_split4(__nv_bfloat16* hi_row, size_t lo_offset, int lane, float4 x) {
+    uint32_t h01, l01, h23, l23;
+    tc::split2_bf16(x.x, x.y, h01, l01);
+    tc::split2_bf16(x.z, x.w, h23, l23);
+    *reinterpret_cast<uint2*>(hi_row + 4 * lane) = make_uint2(h01, h23);
+    *reinterpret_cast<uint2*>(hi_row + lo_offset + 4 * lane) = make_uint2(l01, l23);
+}
+
+__global__ void __launch_bounds__(256) gdn_pf_prep_kernel(int64_t T, int64_t Tp, int vh0, int vc, int h0,
                                                           const float* __restrict__ qkv,
                                                           const float* __restrict__ hist,
                                                           const float* __restrict__ conv_w,
                                                           const float* __restrict__ ssm_a,
                                                           const float* __restrict__ dt_bias,
                                                           const float* __restrict__ alpha,
-                                                          const float* __restrict__ beta, float* __restrict__ qn,
-                                                          float* __restrict__ kn, float* __restrict__ vv,
-                                                          float* __restrict__ gl, float* __restrict__ bt) {
+                                                          const float* __restrict__ beta,
+                                                          __nv_bfloat16* __restrict__ qs, __nv_bfloat16* __restrict__ ks,
+                                                          __nv_bfloat16* __restrict__ vs, float* __restrict__ gl,
+                                                          float* __restrict__ bt) {
     const int64_t t = blockIdx.x;
+    const bool pad = t >= T;     // rows of the last chunk past T: zero operands, g = 0, beta = 0
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float qscale = 1.0f / sqrtf((float)SSM_D);
+    const size_t lo_off = (size_t)Tp * SSM_D;
     for (int gi = warp; gi < 2 * SSM_HK + vc; gi += 8) {
         int cb;
-        if (gi < SSM_HK) cb = gi * SSM_D;                               // q head
-        else if (gi < 2 * SSM_HK) cb = QKD + (gi - SSM_HK) * SSM_D;     // k head
-        else cb = 2 * QKD + (vh0 + gi - 2 * SSM_HK) * SSM_D;            // v head
-        const int ch = cb + 4 * lane;
+        __nv_bfloat16* dst;
+        if (gi < SSM_HK) {                              // q head
+            cb = gi * SSM_D;
+            dst = qs + ((size_t)gi * 2 * Tp + t) * SSM_D;
+        } else if (gi < 2 * SSM_HK) {                   // k head
+            cb = QKD + (gi - SSM_HK) * SSM_D;
+            dst = ks + ((size_t)(gi - SSM_HK) * 2 * Tp + t) * SSM_D;
+        } else {                                        // local v head
+            cb = 2 * QKD + (vh0 + gi - 2 * SSM_HK) * SSM_D;
+            dst = vs + ((size_t)(gi - 2 * SSM_HK) * 2 * Tp + t) * SSM_D;
+        }
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (!pad) {
+            const int ch = cb + 4 * lane;
 #pragma unroll
-        for (int ct = 0; ct < CONV_K; ++ct) {
-            const int64_t st = t + ct - (CONV_K - 1);
-            const float* src = st >= 0 ? qkv + st * QKV_LEN
-                                       : hist + (size_t)((h0 + t + ct + 1) % CONV_K) * QKV_LEN;
-            const float4 x = *reinterpret_cast<const float4*>(src + ch);
-            const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)ct * QKV_LEN + ch);
-            acc.x = fmaf(x.x, w.x, acc.x);
-            acc.y = fmaf(x.y, w.y, acc.y);
-            acc.z = fmaf(x.z, w.z, acc.z);
-            acc.w = fmaf(x.w, w.w, acc.w);
+            for (int ct = 0; ct < CONV_K; ++ct) {
+                const int64_t st = t + ct - (CONV_K - 1);
+                const float* src = st >= 0 ? qkv + st * QKV_LEN
+                                           : hist + (size_t)((h0 + t + ct + 1) % CONV_K) * QKV_LEN;
+                const float4 x = *reinterpret_cast<const float4*>(src + ch);
+                const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)ct * QKV_LEN + ch);
+                acc.x = fmaf(x.x, w.x, acc.x);
+                acc.y = fmaf(x.y, w.y, acc.y);
+                acc.z = fmaf(x.z, w.z, acc.z);
+                acc.w = fmaf(x.w, w.w, acc.w);
+            }
+            acc = make_float4(siluf_acc(acc.x), siluf_acc(acc.y), siluf_acc(acc.z), siluf_acc(acc.w));
+            if (gi < 2 * SSM_HK) {
+                const float ss = warp_sum(acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w);
+                const float inv = 1.0f / sqrtf(ss + 1e-6f);
+                acc = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+                if (gi < SSM_HK) acc = make_float4(acc.x * qscale, acc.y * qscale, acc.z * qscale, acc.w * qscale);
+            }
         }
-        acc = make_float4(siluf_acc(acc.x), siluf_acc(acc.y), siluf_acc(acc.z), siluf_acc(acc.w));
-        if (gi < 2 * SSM_HK) {
-            const float ss = warp_sum(acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w);
-            float inv = 1.0f / sqrtf(ss + 1e-6f);
-            const bool is_q = gi < SSM_HK;
-            const int kh = is_q ? gi : gi - SSM_HK;
-            acc = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-            if (is_q) acc = make_float4(acc.x * qscale, acc.y * qscale, acc.z * qscale, acc.w * qscale);
-            float* dst = (is_q ? qn : kn) + ((size_t)t * SSM_HK + kh) * SSM_D;
-            reinterpret_cast<float4*>(dst)[lane] = acc;
-        } else {
-            const int vl = gi - 2 * SSM_HK;
-            reinterpret_cast<float4*>(vv + ((size_t)t * vc + vl) * SSM_D)[lane] = acc;
-        }
+        store_split4(dst, lo_off, lane, acc);
     }
     for (int vl = threadIdx.x; vl < vc; vl += blockDim.x) {
         const int vh = vh0 + vl;
-        gl[(size_t)t * vc + vl] = ssm_a[vh] * softplus_ref(alpha[(size_t)t * SSM_HV + vh] + dt_bias[vh]);
-        bt[(size_t)t * vc + vl] = sigmoidf_acc(beta[(size_t)t * SSM_HV + vh]);
+        gl[(size_t)vl * Tp + t] = pad ? 0.0f : ssm_a[vh] * softplus_ref(alpha[(size_t)t * SSM_HV + vh] + dt_bias[vh]);
+        bt[(size_t)vl * Tp + t] = pad ? 0.0f : sigmoidf_acc(beta[(size_t)t * SSM_HV + vh]);
     }
 }
 
@@ -116,91 +136,94 @@ __global__ void gdn_pf_ring_kernel(int64_t T, int h0, const float* __restrict__ 
             reinterpret_cast<const float4*>(qkv + (size_t)t * QKV_LEN)[c];
 }
 
-// ---------------------------------------------------------------------------
-// warp-level tensor-core tiles: mma m16n8k8 TF32 with f32 accumulation and a
-// three-product hi/lo split (a*b ~ ah*bh + ah*bl + al*bh) that keeps the
-// products at f32-level accuracy.  Fragment maps (g = lane/4, t = lane%4):
-//   A[m][k]: a0 (g,t) a1 (g+8,t) a2 (g,t+4) a3 (g+8,t+4)
-//   B[k][n]: b0 (t,g) b1 (t+4,g)        C: c0 (g,2t) c1 (g,2t+1) c2 (g+8,2t) c3 (g+8,2t+1)
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
-// hi = the 19 leading bits (what a TF32 operand keeps), lo = the exact
-// remainder; the MMA itself drops the low bits of lo.
-struct FA { uint32_t h[4], l[4]; };
-struct FB { uint32_t h[2], l[2]; };
-__device__ __forceinline__ void split1(float x, uint32_t& h, uint32_t& l) {
-    h = __float_as_uint(x) & 0xFFFFE000u;
-    l = __float_as_uint(x - __uint_as_float(h));
-}
-__device__ __forceinline__ FA split_a(float a0, float a1, float a2, float a3) {
-    FA f;
-    split1(a0, f.h[0], f.l[0]);
-    split1(a1, f.h[1], f.l[1]);
-    split1(a2, f.h[2], f.l[2]);
-    split1(a3, f.h[3], f.l[3]);
-    return f;
-}
-__device__ __forceinline__ FB split_b(float b0, float b1) {
-    FB f;
-    split1(b0, f.h[0], f.l[0]);
-    split1(b1, f.h[1], f.l[1]);
-    return f;
-}
-__device__ __forceinline__ void mma3(float (&d)[4], const FA& a, const FB& b) {
-    mma_tf32(d, a.l, b.h);
-    mma_tf32(d, a.h, b.l);
-    mma_tf32(d, a.h, b.h);
+template <typename S>
+__device__ __forceinline__ S& align1024(unsigned char* raw) {
+    return *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
 }
 
 // ---------------------------------------------------------------------------
-// intra-chunk WY transform, one CTA (8 warps) per (chunk, local v head)
+// intra-chunk WY transform: one CTA (8 warps) per (chunk, local v head)
 // ---------------------------------------------------------------------------
 namespace gp {
-constexpr int SM = C + 4;    // 64-wide matrices read as A fragments
-}
-struct IntraSmem {
-    float K[gp::C][gp::SA];
-    float Q[gp::C][gp::SA];
-    float V[gp::C][gp::SB];
-    float Am[gp::C][gp::SM];   // strictly lower beta_t Gam_ts k_t.k_s
-    float Tm[gp::C][gp::SM];   // (I + Am)^-1
-    float G[gp::C], b[gp::C], eG[gp::C], cw[gp::C], cu[gp::C];
+constexpr int TP = C + 4;        // padded f32 row for the 64x64 triangular solve
+struct alignas(1024) IntraSmem {
+    // [hi|lo][d-box][row][64]: rows 0-63 = K of the chunk, 64-127 = Q.  After the
+    // W / U0 products this 64 KB holds the W images (32 KB) then the U0^T image.
+    __nv_bfloat16 kq[2][2][128][64];
+    __nv_bfloat16 v[2][2][64][64];    // [hi|lo][d-box][s][64]
+    __nv_bfloat16 tmw[2][64][64];     // Tm diag(beta e^G), [hi|lo][t][s] K-major
+    __nv_bfloat16 tmb[2][64][64];     // Tm diag(beta)
+    __nv_bfloat16 p[2][64][64];       // P image [hi|lo][t][s]
+    float am[C][TP];                  // strictly lower beta_t Gam_ts k_t.k_s
+    float tm[C][TP];                  // (I + A)^-1
+    float g[C], b[C], G[C], eG[C];
+    uint64_t bar_in, bar_m1, bar_m2;
+    uint32_t tmem_base;
 };
+// TMEM columns of the intra kernel
+constexpr uint32_t I_KQ = 0, I_W = 64, I_U0 = 128;
+}  // namespace gp
 
-__global__ void __launch_bounds__(256) gdn_pf_intra_kernel(int64_t T, int vh0, int vc, const float* __restrict__ qn,
-                                                           const float* __restrict__ kn, const float* __restrict__ vv,
-                                                           const float* __restrict__ gl, const float* __restrict__ bt,
-                                                           float* __restrict__ rec) {
+__global__ void __launch_bounds__(256, 1) gdn_pf_intra_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                              const __grid_constant__ CUtensorMap tm_k,
+                                                              const __grid_constant__ CUtensorMap tm_v, int64_t Tp,
+                                                              int vh0, int vc, const float* __restrict__ gl,
+                                                              const float* __restrict__ bt,
+                                                              unsigned char* __restrict__ rec, int* err) {
     using namespace gp;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    IntraSmem& sm = *reinterpret_cast<IntraSmem*>(smem_raw);
+    using namespace tc;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    IntraSmem& sm = align1024<IntraSmem>(smem_raw);
     const int c = blockIdx.x, vl = blockIdx.y, tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
-    const int vh = vh0 + vl, kh = vh % SSM_HK;
-    const int64_t t0 = (int64_t)c * C;
-    const int n = (int)(T - t0 < C ? T - t0 : C);
-    float* out = rec + ((size_t)c * vc + vl) * REC;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int kh = (vh0 + vl) % SSM_HK;
+    const int t0 = c * C;
 
-    for (int i = tid; i < C * (D / 4); i += 256) {
-        const int r = i / (D / 4), c4 = i % (D / 4);
-        float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = k4, v4 = k4;
-        if (r < n) {
-            k4 = reinterpret_cast<const float4*>(kn + ((size_t)(t0 + r) * SSM_HK + kh) * D)[c4];
-            q4 = reinterpret_cast<const float4*>(qn + ((size_t)(t0 + r) * SSM_HK + kh) * D)[c4];
-            v4 = reinterpret_cast<const float4*>(vv + ((size_t)(t0 + r) * vc + vl) * D)[c4];
-        }
-        *reinterpret_cast<float4*>(&sm.K[r][4 * c4]) = k4;
-        *reinterpret_cast<float4*>(&sm.Q[r][4 * c4]) = q4;
-        *reinterpret_cast<float4*>(&sm.V[r][4 * c4]) = v4;
+    if (warp == 0) tmem_alloc(&sm.tmem_base, 256);
+    if (tid == 0) {
+        mbar_init(&sm.bar_in, 1);
+        mbar_init(&sm.bar_m1, 1);
+        mbar_init(&sm.bar_m2, 1);
+        fence_mbar_init();
     }
-    if (warp == 0) {   // inclusive cumsum of the 64 log decays (2 per lane)
-        const float a0 = lane * 2 < n ? gl[(size_t)(t0 + 2 * lane) * vc + vl] : 0.0f;
-        const float a1 = lane * 2 + 1 < n ? gl[(size_t)(t0 + 2 * lane + 1) * vc + vl] : 0.0f;
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = sm.tmem_base;
+    bool ok = true;
+
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&sm.bar_in, 12 * 8192 + 2 * 256);
+        for (int hl = 0; hl < 2; ++hl)
+            for (int db = 0; db < 2; ++db) {
+                tma_load_4d(&sm.kq[hl][db][0][0], &tm_k, 64 * db, t0, hl, kh, &sm.bar_in);
+                tma_load_4d(&sm.kq[hl][db][64][0], &tm_q, 64 * db, t0, hl, kh, &sm.bar_in);
+                tma_load_4d(&sm.v[hl][db][0][0], &tm_v, 64 * db, t0, hl, vl, &sm.bar_in);
+            }
+        bulk_g2s(sm.g, gl + (size_t)vl * Tp + t0, 256, &sm.bar_in);
+        bulk_g2s(sm.b, bt + (size_t)vl * Tp + t0, 256, &sm.bar_in);
+    }
+    wait_or_flag(&sm.bar_in, 0, err, ok);
+
+    // ---- [K; Q] K^T  (M 128, N 64, K 128; three split products)
+    if (tid == 0 && ok) {
+        fence_after_sync();
+        constexpr uint32_t ID = idesc_bf16(128, 64, false);
+        const uint32_t kq_hi = smem_u32(&sm.kq[0][0][0][0]), kq_lo = smem_u32(&sm.kq[1][0][0][0]);
+        uint32_t acc = 0;
+        for (int pass = 0; pass < 3; ++pass) {
+            const uint32_t a = pass == 2 ? kq_lo : kq_hi, b = pass == 1 ? kq_lo : kq_hi;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t off = (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u;
+                umma_ss(tmem + I_KQ, sw128_desc(a + off, 16, 1024), sw128_desc(b + off, 16, 1024), ID, acc);
+                acc = 1;
+            }
+        }
+        umma_commit(&sm.bar_m1);
+    }
+    if (warp == 1) {   // inclusive cumsum of the 64 log decays (2 per lane)
+        const float a0 = sm.g[2 * lane], a1 = sm.g[2 * lane + 1];
         float s = a0 + a1;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -210,72 +233,60 @@ __global__ void __launch_bounds__(256) gdn_pf_intra_kernel(int64_t T, int vh0, i
         const float excl = s - (a0 + a1);
         sm.G[2 * lane] = excl + a0;
         sm.G[2 * lane + 1] = excl + a0 + a1;
-        sm.b[2 * lane] = lane * 2 < n ? bt[(size_t)(t0 + 2 * lane) * vc + vl] : 0.0f;
-        sm.b[2 * lane + 1] = lane * 2 + 1 < n ? bt[(size_t)(t0 + 2 * lane + 1) * vc + vl] : 0.0f;
+        sm.eG[2 * lane] = expf(excl + a0);
+        sm.eG[2 * lane + 1] = expf(excl + a0 + a1);
     }
     __syncthreads();
-    const float G_last = sm.G[n - 1];
-    if (tid < C) {
-        const float e = expf(sm.G[tid]);
-        sm.eG[tid] = e;
-        sm.cw[tid] = sm.b[tid] * e;    // W coefficients   beta e^G
-        sm.cu[tid] = sm.b[tid];        // U0 coefficients  beta
-    }
-    __syncthreads();
-    // X rows 64..127 = Q e^G ; Kd = K e^{G_last - G}
-    for (int i = tid; i < C * (D / 4); i += 256) {
-        const int r = i / (D / 4), c4 = i % (D / 4);
-        const float eq = sm.eG[r], ek = expf(G_last - sm.G[r]);
-        const float4 q4 = *reinterpret_cast<const float4*>(&sm.Q[r][4 * c4]);
-        const float4 k4 = *reinterpret_cast<const float4*>(&sm.K[r][4 * c4]);
-        *reinterpret_cast<float4*>(out + OFF_X + (size_t)(C + r) * SA + 4 * c4) =
-            make_float4(q4.x * eq, q4.y * eq, q4.z * eq, q4.w * eq);
-        *reinterpret_cast<float4*>(out + OFF_KD + (size_t)r * SB + 4 * c4) =
-            make_float4(k4.x * ek, k4.y * ek, k4.z * ek, k4.w * ek);
-    }
-    if (tid == 0) out[OFF_EG] = expf(G_last);
 
-    // ---- [K; Q] K^T on tensor tiles: warp w owns stacked rows 16w..16w+15, 8 n-tiles
-    {
-        const int m0 = (warp & 3) * 16;
-        float (*A)[SA] = warp < 4 ? sm.K : sm.Q;
-        float acc[8][4];
+    // ---- epilogue 1: rows 0-63 -> A (f32, for the solve), rows 64-127 -> P image
+    const int q4 = warp & 3, h = warp >> 2;
+    const int row = 32 * q4 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
+    if (wait_or_flag(&sm.bar_m1, 0, err, ok)) {
+        fence_after_sync();
+        float x[32];
+        tmem_ld32(lane_addr + I_KQ + 32 * h, x);
+        if (row < C) {
+            const int t = row;
+            const float bt_ = sm.b[t], Gt = sm.G[t];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+            for (int j = 0; j < 32; ++j) {
+                const int s = 32 * h + j;
+                sm.am[t][s] = s < t ? bt_ * expf(Gt - sm.G[s]) * x[j] : 0.0f;
+            }
+        } else {
+            const int t = row - C;
+            const float Gt = sm.G[t];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
-#pragma unroll 2
-        for (int k0 = 0; k0 < D; k0 += 8) {
-            const FA a = split_a(A[m0 + g][k0 + t4], A[m0 + g + 8][k0 + t4], A[m0 + g][k0 + t4 + 4],
-                                 A[m0 + g + 8][k0 + t4 + 4]);
+            for (int j8 = 0; j8 < 4; ++j8) {
+                uint4 hi, lo;
+                uint32_t* hp = &hi.x;
+                uint32_t* lp = &lo.x;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) mma3(acc[j], a, split_b(sm.K[8 * j + g][k0 + t4], sm.K[8 * j + g][k0 + t4 + 4]));
-        }
-        // epilogue: rows of K K^T -> Am (strict lower, beta Gam); rows of Q K^T -> P (lower incl.)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int i = m0 + g + (e >> 1) * 8;
-                const int s = 8 * j + 2 * t4 + (e & 1);
-                const float gam = s <= i ? expf(sm.G[i] - sm.G[s]) : 0.0f;
-                if (warp < 4) sm.Am[i][s] = s < i ? sm.b[i] * gam * acc[j][e] : 0.0f;
-                else out[OFF_P + i * SP + s] = gam * acc[j][e];
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 8 * j8 + 2 * e, s = 32 * h + j;
+                    const float p0 = s <= t ? expf(Gt - sm.G[s]) * x[j] : 0.0f;
+                    const float p1 = s + 1 <= t ? expf(Gt - sm.G[s + 1]) * x[j + 1] : 0.0f;
+                    split2_bf16(p0, p1, hp[e], lp[e]);
+                }
+                const uint32_t off = sw128_off_b16((uint32_t)t, (uint32_t)(32 * h + 8 * j8));
+                *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.p[0][0][0]) + off) = hi;
+                *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.p[1][0][0]) + off) = lo;
             }
         }
     }
     __syncthreads();
-    // ---- Tm = (I + Am)^-1, blocked 16x16.  Diagonal blocks: warp b, forward substitution.
+
+    // ---- Tm = (I + A)^-1, blocked 16x16.  Diagonal blocks: warp b, forward substitution.
     if (warp < 4) {
         const int b0 = 16 * warp;
         for (int i = 0; i < 16; ++i) {
             if (lane < 16) {
                 const int j = lane;
-                float x = (i == j) ? 1.0f : 0.0f;
-                for (int s = j; s < i; ++s) x = fmaf(-sm.Am[b0 + i][b0 + s], sm.Tm[b0 + s][b0 + j], x);
-                sm.Tm[b0 + i][b0 + j] = (j <= i) ? x : 0.0f;
-                // zero the strictly upper blocks of this block row
-                for (int jj = b0 + 16; jj < C; jj += 16) sm.Tm[b0 + i][jj + j] = 0.0f;
+                float xv = (i == j) ? 1.0f : 0.0f;
+                for (int s = j; s < i; ++s) xv = fmaf(-sm.am[b0 + i][b0 + s], sm.tm[b0 + s][b0 + j], xv);
+                sm.tm[b0 + i][b0 + j] = (j <= i) ? xv : 0.0f;
+                for (int jj = b0 + 16; jj < C; jj += 16) sm.tm[b0 + i][jj + j] = 0.0f;   // strictly upper blocks
             }
             __syncwarp();
         }
@@ -285,272 +296,553 @@ __global__ void __launch_bounds__(256) gdn_pf_intra_kernel(int64_t T, int vh0, i
     for (int d = 1; d < 4; ++d) {
         if (warp < 4 - d) {
             const int J = warp, I = warp + d;
-            float m[8];
-            // lane computes 8 entries of M (16x16): rows r = lane/2, cols 8*(lane%2)..+8
             const int r = lane >> 1, cb = 8 * (lane & 1);
+            float m[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) m[e] = 0.0f;
             for (int Kb = J; Kb < I; ++Kb)
                 for (int s = 0; s < 16; ++s) {
-                    const float a = sm.Am[16 * I + r][16 * Kb + s];
+                    const float a = sm.am[16 * I + r][16 * Kb + s];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) m[e] = fmaf(a, sm.Tm[16 * Kb + s][16 * J + cb + e], m[e]);
+                    for (int e = 0; e < 8; ++e) m[e] = fmaf(a, sm.tm[16 * Kb + s][16 * J + cb + e], m[e]);
                 }
-            // stash M in the (still zero) target block, then T_IJ = -T_II M
 #pragma unroll
-            for (int e = 0; e < 8; ++e) sm.Tm[16 * I + r][16 * J + cb + e] = m[e];
+            for (int e = 0; e < 8; ++e) sm.tm[16 * I + r][16 * J + cb + e] = m[e];
             __syncwarp();
             float o[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) o[e] = 0.0f;
             for (int s = 0; s <= r; ++s) {
-                const float tii = sm.Tm[16 * I + r][16 * I + s];
+                const float tii = sm.tm[16 * I + r][16 * I + s];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) o[e] = fmaf(tii, sm.Tm[16 * I + s][16 * J + cb + e], o[e]);
+                for (int e = 0; e < 8; ++e) o[e] = fmaf(tii, sm.tm[16 * I + s][16 * J + cb + e], o[e]);
             }
             __syncwarp();
 #pragma unroll
-            for (int e = 0; e < 8; ++e) sm.Tm[16 * I + r][16 * J + cb + e] = -o[e];
+            for (int e = 0; e < 8; ++e) sm.tm[16 * I + r][16 * J + cb + e] = -o[e];
         }
         __syncthreads();
     }
-    // ---- [W | U0] = Tm [beta e^G K | beta V]  (64 x 256): warp -> m-tile (warp&3), 16 n-tiles of half (warp>>2)
-    {
-        const int m0 = (warp & 3) * 16;
-        const bool is_u = warp >= 4;
-        const float* coef = is_u ? sm.cu : sm.cw;
-        float acc[16][4];
+    // ---- Tm diag(beta e^G) and Tm diag(beta) as split K-major images [t][s]
+    for (int i = tid; i < C * 8; i += 256) {
+        const int t = i >> 3, j8 = i & 7;
+        uint4 wh, wl, bh, bl;
+        uint32_t *whp = &wh.x, *wlp = &wl.x, *bhp = &bh.x, *blp = &bl.x;
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[j][e] = 0.0f;
-        for (int k0 = 0; k0 < C; k0 += 8) {
-            const FA a = split_a(sm.Tm[m0 + g][k0 + t4], sm.Tm[m0 + g + 8][k0 + t4], sm.Tm[m0 + g][k0 + t4 + 4],
-                                 sm.Tm[m0 + g + 8][k0 + t4 + 4]);
-            const float c0 = coef[k0 + t4], c1 = coef[k0 + t4 + 4];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const FB bb = is_u ? split_b(c0 * sm.V[k0 + t4][8 * j + g], c1 * sm.V[k0 + t4 + 4][8 * j + g])
-                                   : split_b(c0 * sm.K[k0 + t4][8 * j + g], c1 * sm.K[k0 + t4 + 4][8 * j + g]);
-                mma3(acc[j], a, bb);
-            }
+        for (int e = 0; e < 4; ++e) {
+            const int s = 8 * j8 + 2 * e;
+            const float a0 = sm.tm[t][s], a1 = sm.tm[t][s + 1];
+            const float cb0 = sm.b[s], cb1 = sm.b[s + 1];
+            split2_bf16(a0 * cb0 * sm.eG[s], a1 * cb1 * sm.eG[s + 1], whp[e], wlp[e]);
+            split2_bf16(a0 * cb0, a1 * cb1, bhp[e], blp[e]);
         }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int i = m0 + g + 8 * h;
-                const int col = 8 * j + 2 * t4;
-                const float2 v2 = make_float2(acc[j][2 * h], acc[j][2 * h + 1]);
-                if (is_u) {   // U0 stored v-block major: [col/VB][i][col%VB]
-                    *reinterpret_cast<float2*>(out + OFF_U0 + ((size_t)(col / VB) * C + i) * VB + (col % VB)) = v2;
-                } else {
-                    *reinterpret_cast<float2*>(out + OFF_X + (size_t)i * SA + col) = v2;
-                }
-            }
-        }
+        const uint32_t off = sw128_off_b16((uint32_t)t, (uint32_t)(8 * j8));
+        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.tmw[0][0][0]) + off) = wh;
+        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.tmw[1][0][0]) + off) = wl;
+        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.tmb[0][0][0]) + off) = bh;
+        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.tmb[1][0][0]) + off) = bl;
     }
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    // ---- W^T = K^T TmW^T and U0^T = V^T TmB^T  (M 128 over k / v, N 64, K 64; A MN-major)
+    if (tid == 0 && ok) {
+        fence_after_sync();
+        constexpr uint32_t ID = idesc_bf16(128, 64, false, true);
+        const uint32_t k_hi = smem_u32(&sm.kq[0][0][0][0]), k_lo = smem_u32(&sm.kq[1][0][0][0]);
+        const uint32_t v_hi = smem_u32(&sm.v[0][0][0][0]), v_lo = smem_u32(&sm.v[1][0][0][0]);
+        const uint32_t w_hi = smem_u32(&sm.tmw[0][0][0]), w_lo = smem_u32(&sm.tmw[1][0][0]);
+        const uint32_t b_hi = smem_u32(&sm.tmb[0][0][0]), b_lo = smem_u32(&sm.tmb[1][0][0]);
+        uint32_t acc = 0;
+        for (int pass = 0; pass < 3; ++pass) {
+            const uint32_t a = pass == 2 ? k_lo : k_hi, b = pass == 1 ? w_lo : w_hi;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                // A: K rows s (128 B of d each), d blocks of 64 in the 16 KB d-boxes
+                umma_ss(tmem + I_W, sw128_desc(a + (uint32_t)ks * 2048u, 16384, 1024),
+                        sw128_desc(b + (uint32_t)ks * 32u, 16, 1024), ID, acc);
+                acc = 1;
+            }
+        }
+        acc = 0;
+        for (int pass = 0; pass < 3; ++pass) {
+            const uint32_t a = pass == 2 ? v_lo : v_hi, b = pass == 1 ? b_lo : b_hi;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                umma_ss(tmem + I_U0, sw128_desc(a + (uint32_t)ks * 2048u, 8192, 1024),
+                        sw128_desc(b + (uint32_t)ks * 32u, 16, 1024), ID, acc);
+                acc = 1;
+            }
+        }
+        umma_commit(&sm.bar_m2);
+    }
+    unsigned char* img = reinterpret_cast<unsigned char*>(&sm.kq[0][0][0][0]);   // W images, then U0^T image
+    if (wait_or_flag(&sm.bar_m2, 0, err, ok)) {
+        fence_after_sync();
+        float x[32];
+        // W^T: lane = k, columns t in [32h, 32h + 32) -> W[t][k] images
+        tmem_ld32(lane_addr + I_W + 32 * h, x);
+        {
+            const uint32_t kb = (uint32_t)row >> 6, kc = (uint32_t)row & 63u;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                __nv_bfloat16 hi, lo;
+                split_bf16(x[j], hi, lo);
+                const uint32_t off = kb * 8192u + sw128_off_b16((uint32_t)(32 * h + j), kc);
+                *reinterpret_cast<__nv_bfloat16*>(img + off) = hi;
+                *reinterpret_cast<__nv_bfloat16*>(img + 16384 + off) = lo;
+            }
+        }
+        // U0^T: lane = v, columns t in [32h, 32h + 32) -> t-box h of the f32 image
+        tmem_ld32(lane_addr + I_U0 + 32 * h, x);
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4)
+            *reinterpret_cast<float4*>(img + REC_U0 + (uint32_t)h * 16384u + sw128_off_b32((uint32_t)row, 4u * j4)) =
+                make_float4(x[4 * j4], x[4 * j4 + 1], x[4 * j4 + 2], x[4 * j4 + 3]);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0 && ok) {
+        unsigned char* R = rec + ((size_t)c * vc + vl) * REC_BYTES;
+        bulk_s2g(R + REC_W, img, 65536);
+        bulk_s2g(R + REC_P, &sm.p[0][0][0], 16384);
+        bulk_s2g(R + REC_G, sm.G, 256);
+        bulk_commit();
+        bulk_wait_all();
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 // ---------------------------------------------------------------------------
-// inter-chunk recurrence: one CTA (4 warps) per (VB-row block of S, local v head).
-// Chunk operands stream into shared memory with 1-D bulk async copies in two
-// groups (A = X and the U0 slice, B = P and Kd), each refilled for the next
-// chunk as soon as the current chunk has finished with it.
-//   step 1 (all warps, 32 rows each):  [W; Q e^G] S^T  -> U (rows 0..63), Yp (64..127)
-//   step 2 (warps 2, 3):              Y = Yp + P U
-//   step 3 (all warps, 32 columns each): S = e^{G_last} S + U^T Kd
+// chunk recurrence: one persistent CTA per local v head
 // ---------------------------------------------------------------------------
 namespace gp {
-constexpr int SU = VB + 8;   // U rows: conflict-free as row-major B and as transposed A
-constexpr int NT1 = VB / 8;  // n-tiles of step 1 / 2
-}
-struct InterSmem {
-    float X[2 * gp::C][gp::SA];   // [W; Q e^G]
-    float Kd[gp::C][gp::SB];
-    float P[gp::C][gp::SP];
-    float U0[gp::C][gp::VB];
-    float S[gp::VB][gp::SA];      // state rows [v][k]
-    float U[gp::C][gp::SU];
-    uint64_t barA, barB;
+struct alignas(1024) ChainSmem {
+    unsigned char w[32768];      // record: W images [hi|lo][k-box][64 t][64 k]
+    unsigned char u0t[32768];    // record: U0^T image [t-box][128 v][32 t]
+    unsigned char p[16384];      // record: P images [hi|lo][64 t][64 s]
+    unsigned char qe[32768];     // Q [hi|lo][d-box][64 t][64 d] as loaded, scaled in place to Q e^G
+    unsigned char kd[32768];     // K e^{G_last - G}, same layout (B operand, MN-major)
+    unsigned char kraw[32768];   // K as loaded
+    float zt[C][D];              // z rows of the chunk for this head [t][v] (TMA, zero past T)
+    float gring[4][C];           // G of chunks c % 4
+    float red[4][C];             // per-warp partial sums of y^2 per token
+    float inv[C];                // 1 / rms per token
+    uint64_t full_w, full_u0, full_p, full_q, full_k, full_z, full_g[4];
+    uint64_t mma1_done, dy1_done, mma3_done;
+    uint64_t mma2_done[2], y_free[2];   // per D_Y buffer (chunk parity): one completion every 2 chunks
+    uint64_t s_ready, u_ready, qe_ready, kd_ready, z_free;
+    uint32_t tmem_base;
 };
+// TMEM columns of the chain kernel (512 allocated)
+constexpr uint32_t S_ACC = 0;    // f32 state [v lane][k], holds e^{G_last} S between the S epilogue and MMA3
+constexpr uint32_t S_HI = 128;   // bf16 pairs of S (A operand), 64 columns
+constexpr uint32_t S_LO = 192;
+constexpr uint32_t D_U = 256;    // S W^T, f32 [v][t]
+constexpr uint32_t U_HI = 320;   // bf16 pairs of U^T (A operand), 32 columns
+constexpr uint32_t U_LO = 352;
+constexpr uint32_t D_Y = 384;    // Y^T f32 [v][t], two buffers (chunk parity) at 384 and 448
+// warp roles
+constexpr int EY_W0 = 0;         // warps 0-3: y epilogue (gated RMSNorm, store)
+constexpr int E1_W0 = 4;         // warps 4-11: U and S epilogues (the serial path)
+constexpr int ES_W0 = 12;        // warps 12-15: Q e^G and K e^{G_last - G} scaling
+constexpr int CTL_W = 16;        // warp 16: lane 0 loads, lane 1 issues MMAs
+constexpr int CHAIN_THREADS = 17 * 32;
+}  // namespace gp
 
-__device__ __forceinline__ void inter_issue_A(InterSmem& sm, const float* R, int vb, int lane) {
-    using namespace gp;
-    if (lane == 0) {
-        mbar_arrive_expect_tx(&sm.barA, 2 * C * SA * 4 + C * VB * 4);
-        bulk_g2s(&sm.X[0][0], R + OFF_X, 2 * C * SA * 4, &sm.barA);
-        bulk_g2s(&sm.U0[0][0], R + OFF_U0 + (size_t)vb * C * VB, C * VB * 4, &sm.barA);
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(nthreads) : "memory");
+    return r != 0;
+}
+
+// One halving step of a warp reduce-scatter: N values per lane -> N/2, lanes
+// with BIT set keep (and sum) the upper half.
+template <int N, int BIT>
+__device__ __forceinline__ void bfly_reduce(float* a, int lane) {
+    const bool up = (lane & BIT) != 0;
+#pragma unroll
+    for (int j = 0; j < N / 2; ++j) {
+        const float keep = up ? a[j + N / 2] : a[j];
+        const float send = up ? a[j] : a[j + N / 2];
+        a[j] = keep + __shfl_xor_sync(0xffffffffu, send, BIT);
     }
 }
-__device__ __forceinline__ void inter_issue_B(InterSmem& sm, const float* R, int lane) {
-    using namespace gp;
-    if (lane == 0) {
-        mbar_arrive_expect_tx(&sm.barB, C * SB * 4 + C * SP * 4);
-        bulk_g2s(&sm.Kd[0][0], R + OFF_KD, C * SB * 4, &sm.barB);
-        bulk_g2s(&sm.P[0][0], R + OFF_P, C * SP * 4, &sm.barB);
+
+// scale each 128-byte row t of a [hi|lo][d-box][64][64] bf16 image by f(t), re-splitting hi/lo
+template <typename F>
+__device__ __forceinline__ void scale_rows(const unsigned char* src, unsigned char* dst, int tid, int nthr, F f) {
+    for (int i = tid; i < 1024; i += nthr) {          // 16-byte chunks of the hi image
+        const uint32_t off = (uint32_t)i * 16u;
+        const int t = (int)((off & 8191u) >> 7);
+        const float sc = f(t);
+        const uint4 h = *reinterpret_cast<const uint4*>(src + off);
+        const uint4 l = *reinterpret_cast<const uint4*>(src + 16384 + off);
+        const uint32_t* hp = &h.x;
+        const uint32_t* lp = &l.x;
+        uint4 nh, nl;
+        uint32_t* nhp = &nh.x;
+        uint32_t* nlp = &nl.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float a = (tc::bf16_lo_f(hp[e]) + tc::bf16_lo_f(lp[e])) * sc;
+            const float b = (tc::bf16_hi_f(hp[e]) + tc::bf16_hi_f(lp[e])) * sc;
+            tc::split2_bf16(a, b, nhp[e], nlp[e]);
+        }
+        *reinterpret_cast<uint4*>(dst + off) = nh;
+        *reinterpret_cast<uint4*>(dst + 16384 + off) = nl;
     }
 }
 
-__global__ void __launch_bounds__(128) gdn_pf_inter_kernel(int64_t T, int vc, const float* __restrict__ rec,
-                                                           float* __restrict__ state, float* __restrict__ yraw,
-                                                           int* err) {
+__global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_z, int64_t T, int NC, int vh0, int vc, const unsigned char* __restrict__ rec,
+    float* __restrict__ state, const float* __restrict__ norm_w, float* __restrict__ y_out, int* err) {
     using namespace gp;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    InterSmem& sm = *reinterpret_cast<InterSmem*>(smem_raw);
-    const int vb = blockIdx.x, vl = blockIdx.y, tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
-    float* Sg = state + ((size_t)vl * D + (size_t)vb * VB) * D;
-    const int NC = (int)((T + C - 1) / C);
+    using namespace tc;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    ChainSmem& sm = align1024<ChainSmem>(smem_raw);
+    const int vl = blockIdx.x, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int kh = (vh0 + vl) % SSM_HK;
+    auto R = [&](int c) { return rec + ((size_t)c * vc + vl) * REC_BYTES; };
+
+    if (warp == CTL_W) tmem_alloc(&sm.tmem_base, 512);
     if (tid == 0) {
-        mbar_init(&sm.barA, 1);
-        mbar_init(&sm.barB, 1);
+        uint64_t* one[11] = {&sm.full_w, &sm.full_u0, &sm.full_p, &sm.full_q, &sm.full_k, &sm.full_z,
+                             &sm.mma1_done, &sm.dy1_done, &sm.mma3_done, &sm.mma2_done[0], &sm.mma2_done[1]};
+        for (uint64_t* b : one) mbar_init(b, 1);
+        for (int i = 0; i < 4; ++i) mbar_init(&sm.full_g[i], 1);
+        mbar_init(&sm.s_ready, 256);
+        mbar_init(&sm.u_ready, 256);
+        mbar_init(&sm.qe_ready, 128);
+        mbar_init(&sm.kd_ready, 128);
+        mbar_init(&sm.y_free[0], 128);
+        mbar_init(&sm.y_free[1], 128);
+        mbar_init(&sm.z_free, 128);
         fence_mbar_init();
     }
-    for (int i = tid; i < VB * (D / 4); i += 128) {
-        const int r = i / (D / 4), c4 = i % (D / 4);
-        *reinterpret_cast<float4*>(&sm.S[r][4 * c4]) = reinterpret_cast<const float4*>(Sg + (size_t)r * D)[c4];
-    }
+    fence_before_sync();
     __syncthreads();
-    if (warp == 0) {
-        const float* R0 = rec + (size_t)vl * REC;
-        inter_issue_A(sm, R0, vb, lane);
-        inter_issue_B(sm, R0, lane);
-    }
+    fence_after_sync();
+    const uint32_t tmem = sm.tmem_base;
     bool ok = true;
-    for (int c = 0; c < NC; ++c) {
-        const float* R = rec + ((size_t)c * vc + vl) * REC;
-        const int64_t t0 = (int64_t)c * C;
-        const int n = (int)(T - t0 < C ? T - t0 : C);
-        // ---- step 1
-        if (!mbar_wait(&sm.barA, (uint32_t)(c & 1), err)) ok = false;
-        if (__syncthreads_or(!ok)) break;
-        float acc[2][NT1][4];
-#pragma unroll
-        for (int mi = 0; mi < 2; ++mi)
-#pragma unroll
-            for (int j = 0; j < NT1; ++j)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[mi][j][e] = 0.0f;
-        const int r0 = 32 * warp;
-#pragma unroll 4
-        for (int k0 = 0; k0 < D; k0 += 8) {
-            FB bb[NT1];
-#pragma unroll
-            for (int j = 0; j < NT1; ++j) bb[j] = split_b(sm.S[8 * j + g][k0 + t4], sm.S[8 * j + g][k0 + t4 + 4]);
-#pragma unroll
-            for (int mi = 0; mi < 2; ++mi) {
-                const int m0 = r0 + 16 * mi;
-                const FA a = split_a(sm.X[m0 + g][k0 + t4], sm.X[m0 + g + 8][k0 + t4], sm.X[m0 + g][k0 + t4 + 4],
-                                     sm.X[m0 + g + 8][k0 + t4 + 4]);
-#pragma unroll
-                for (int j = 0; j < NT1; ++j) mma3(acc[mi][j], a, bb[j]);
+
+    if (warp == CTL_W) {
+        if (lane == 0) {
+            // ---------------- loader ----------------
+            for (int c = 0; c < NC && c < 3; ++c) {
+                mbar_arrive_expect_tx(&sm.full_g[c], 256);
+                bulk_g2s(sm.gring[c], R(c) + REC_G, 256, &sm.full_g[c]);
             }
-        }
-        if (warp < 2) {
-#pragma unroll
-            for (int mi = 0; mi < 2; ++mi)
-#pragma unroll
-                for (int j = 0; j < NT1; ++j)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int i = r0 + 16 * mi + g + (e >> 1) * 8;
-                        const int v = 8 * j + 2 * t4 + (e & 1);
-                        sm.U[i][v] = sm.U0[i][v] - acc[mi][j][e];
-                    }
-        }
-        __syncthreads();                      // U complete; X, U0 free
-        if (warp == 0 && c + 1 < NC) inter_issue_A(sm, R + (size_t)vc * REC, vb, lane);
-        if (!mbar_wait(&sm.barB, (uint32_t)(c & 1), err)) ok = false;
-        if (__syncthreads_or(!ok)) break;
-        // ---- step 3 (every warp, columns 32w..32w+31): S_new = e^{G_last} S + U^T Kd
-        float snew[4][4];
-        {
-            const float eGl = __ldg(R + OFF_EG);
-            const int n0w = 32 * warp;
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    snew[j][e] = eGl * sm.S[g + (e >> 1) * 8][n0w + 8 * j + 2 * t4 + (e & 1)];
-#pragma unroll 2
-            for (int k0 = 0; k0 < C; k0 += 8) {
-                const FA a = split_a(sm.U[k0 + t4][g], sm.U[k0 + t4][g + 8], sm.U[k0 + t4 + 4][g],
-                                     sm.U[k0 + t4 + 4][g + 8]);
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    mma3(snew[j], a, split_b(sm.Kd[k0 + t4][n0w + 8 * j + g], sm.Kd[k0 + t4 + 4][n0w + 8 * j + g]));
-            }
-        }
-        // ---- step 2 (warps 2, 3): Y = Yp + P U
-        if (warp >= 2) {
-            const int yi0 = r0 - C;
-#pragma unroll
-            for (int mi = 0; mi < 2; ++mi) {
-                const int m0 = yi0 + 16 * mi;
-#pragma unroll 2
-                for (int k0 = 0; k0 < C; k0 += 8) {
-                    const FA a = split_a(sm.P[m0 + g][k0 + t4], sm.P[m0 + g + 8][k0 + t4], sm.P[m0 + g][k0 + t4 + 4],
-                                         sm.P[m0 + g + 8][k0 + t4 + 4]);
-#pragma unroll
-                    for (int j = 0; j < NT1; ++j)
-                        mma3(acc[mi][j], a, split_b(sm.U[k0 + t4][8 * j + g], sm.U[k0 + t4 + 4][8 * j + g]));
+            for (int c = 0; c < NC && ok; ++c) {
+                const uint32_t pp = (uint32_t)((c - 1) & 1);
+                const int t0 = c * C;
+                if (c > 0 && !wait_or_flag(&sm.kd_ready, pp, err, ok)) break;
+                mbar_arrive_expect_tx(&sm.full_k, 32768);
+                for (int hl = 0; hl < 2; ++hl)
+                    for (int db = 0; db < 2; ++db)
+                        tma_load_4d(sm.kraw + hl * 16384 + db * 8192, &tm_k, 64 * db, t0, hl, kh, &sm.full_k);
+                if (c > 0 && !wait_or_flag(&sm.mma1_done, pp, err, ok)) break;
+                mbar_arrive_expect_tx(&sm.full_w, 32768);
+                bulk_g2s(sm.w, R(c) + REC_W, 32768, &sm.full_w);
+                if (c > 0 && !wait_or_flag(&sm.u_ready, pp, err, ok)) break;
+                mbar_arrive_expect_tx(&sm.full_u0, 32768);
+                bulk_g2s(sm.u0t, R(c) + REC_U0, 32768, &sm.full_u0);
+                if (c > 0 && !wait_or_flag(&sm.dy1_done, pp, err, ok)) break;
+                mbar_arrive_expect_tx(&sm.full_q, 32768);
+                for (int hl = 0; hl < 2; ++hl)
+                    for (int db = 0; db < 2; ++db)
+                        tma_load_4d(sm.qe + hl * 16384 + db * 8192, &tm_q, 64 * db, t0, hl, kh, &sm.full_q);
+                if (c > 0 && !wait_or_flag(&sm.mma2_done[(c - 1) & 1], (uint32_t)(((c - 1) >> 1) & 1), err, ok)) break;
+                mbar_arrive_expect_tx(&sm.full_p, 16384);
+                bulk_g2s(sm.p, R(c) + REC_P, 16384, &sm.full_p);
+                if (c > 0 && !wait_or_flag(&sm.z_free, pp, err, ok)) break;
+                mbar_arrive_expect_tx(&sm.full_z, C * D * 4);
+                tma_load_2d(&sm.zt[0][0], &tm_z, (vh0 + vl) * D, t0, &sm.full_z);
+                // G of chunk c+3 into slot (c+3)%4 (chunk c-1's G: every reader finished before MMA2(c-1))
+                if (c + 3 < NC) {
+                    const int s = (c + 3) & 3;
+                    mbar_arrive_expect_tx(&sm.full_g[s], 256);
+                    bulk_g2s(sm.gring[s], R(c + 3) + REC_G, 256, &sm.full_g[s]);
                 }
+            }
+        } else if (lane == 1) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t ID64 = idesc_bf16(128, 64, false);
+            constexpr uint32_t ID128MN = idesc_bf16(128, 128, true);
+            const uint32_t w_s = smem_u32(sm.w), q_s = smem_u32(sm.qe), k_s = smem_u32(sm.kd), p_s = smem_u32(sm.p);
+            for (int c = 0; c < NC && ok; ++c) {
+                const uint32_t ph = (uint32_t)(c & 1);
+                // U-part: D_U = S W^T  (A = S hi/lo from TMEM, B = W images, N 64, K 128)
+                if (!wait_or_flag(&sm.s_ready, ph, err, ok) || !wait_or_flag(&sm.full_w, ph, err, ok)) break;
+                fence_after_sync();
+                {
+                    uint32_t acc = 0;
+                    for (int pass = 0; pass < 3; ++pass) {
+                        const uint32_t a = pass == 2 ? S_LO : S_HI, b = w_s + (pass == 1 ? 16384u : 0u);
 #pragma unroll
-                for (int j = 0; j < NT1; ++j)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int i = m0 + g + 8 * h;
-                        if (i < n) {
-                            float* yo = yraw + ((size_t)(t0 + i) * vc + vl) * D + vb * VB + 8 * j + 2 * t4;
-                            *reinterpret_cast<float2*>(yo) = make_float2(acc[mi][j][2 * h], acc[mi][j][2 * h + 1]);
+                        for (int ks = 0; ks < 8; ++ks) {
+                            umma_ts(tmem + D_U, tmem + a + 8u * ks,
+                                    sw128_desc(b + (uint32_t)(ks >> 2) * 8192u + (uint32_t)(ks & 3) * 32u, 16, 1024),
+                                    ID64, acc);
+                            acc = 1;
                         }
                     }
+                }
+                umma_commit(&sm.mma1_done);
+                // Y-part 1: D_Y = S Qe^T
+                if (!wait_or_flag(&sm.qe_ready, ph, err, ok)) break;
+                if (c > 1 && !wait_or_flag(&sm.y_free[c & 1], (uint32_t)(((c - 2) >> 1) & 1), err, ok)) break;
+                const uint32_t dy = D_Y + 64u * (uint32_t)(c & 1);
+                fence_after_sync();
+                {
+                    uint32_t acc = 0;
+                    for (int pass = 0; pass < 3; ++pass) {
+                        const uint32_t a = pass == 2 ? S_LO : S_HI, b = q_s + (pass == 1 ? 16384u : 0u);
+#pragma unroll
+                        for (int ks = 0; ks < 8; ++ks) {
+                            umma_ts(tmem + dy, tmem + a + 8u * ks,
+                                    sw128_desc(b + (uint32_t)(ks >> 2) * 8192u + (uint32_t)(ks & 3) * 32u, 16, 1024),
+                                    ID64, acc);
+                            acc = 1;
+                        }
+                    }
+                }
+                umma_commit(&sm.dy1_done);
+                // state: S_ACC (= e^{G_last} S) += U^T Kd  (B = Kd MN-major, N 128, K 64)
+                if (!wait_or_flag(&sm.u_ready, ph, err, ok) || !wait_or_flag(&sm.kd_ready, ph, err, ok)) break;
+                fence_after_sync();
+                for (int pass = 0; pass < 3; ++pass) {
+                    const uint32_t a = pass == 2 ? U_LO : U_HI, b = k_s + (pass == 1 ? 16384u : 0u);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        umma_ts(tmem + S_ACC, tmem + a + 8u * ks, sw128_desc(b + (uint32_t)ks * 2048u, 8192, 1024),
+                                ID128MN, 1);
+                }
+                umma_commit(&sm.mma3_done);
+                // Y-part 2: D_Y += U^T P^T  (B = P images, N 64, K 64)
+                if (!wait_or_flag(&sm.full_p, ph, err, ok)) break;
+                fence_after_sync();
+                for (int pass = 0; pass < 3; ++pass) {
+                    const uint32_t a = pass == 2 ? U_LO : U_HI, b = p_s + (pass == 1 ? 8192u : 0u);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        umma_ts(tmem + dy, tmem + a + 8u * ks, sw128_desc(b + (uint32_t)ks * 32u, 16, 1024), ID64, 1);
+                }
+                umma_commit(&sm.mma2_done[c & 1]);
             }
         }
-        __syncthreads();                      // every read of S, U, P, Kd for this chunk is done
-        {
-            const int n0w = 32 * warp;
+    } else if (warp >= E1_W0 && warp < ES_W0) {
+        // ---------------- U and S epilogues (thread = state row v, half h of the columns) ----------------
+        const int q4 = warp & 3, h = (warp - E1_W0) >> 2;
+        const int v = 32 * q4 + lane;
+        const uint32_t la = tmem + ((uint32_t)(32 * q4) << 16);
+        float* Sg = state + ((size_t)vl * D + v) * D;
+        // initial state: S_HI/S_LO <- split(S0), S_ACC <- e^{G_last(0)} S0
+        if (wait_or_flag(&sm.full_g[0], 0, err, ok)) {
+            const float e0 = expf(sm.gring[0][C - 1]);
+            for (int piece = 0; piece < 2; ++piece) {
+                const int k0 = 64 * h + 32 * piece;
+                uint32_t hi[16], lo[16], sc[32];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-                    *reinterpret_cast<float2*>(&sm.S[g + 8 * h][n0w + 8 * j + 2 * t4]) =
-                        make_float2(snew[j][2 * h], snew[j][2 * h + 1]);
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 s4 = *reinterpret_cast<const float4*>(Sg + k0 + 4 * j4);
+                    split2_bf16(s4.x, s4.y, hi[2 * j4], lo[2 * j4]);
+                    split2_bf16(s4.z, s4.w, hi[2 * j4 + 1], lo[2 * j4 + 1]);
+                    sc[4 * j4] = __float_as_uint(s4.x * e0);
+                    sc[4 * j4 + 1] = __float_as_uint(s4.y * e0);
+                    sc[4 * j4 + 2] = __float_as_uint(s4.z * e0);
+                    sc[4 * j4 + 3] = __float_as_uint(s4.w * e0);
+                }
+                tmem_st16_async(la + S_HI + (uint32_t)(k0 >> 1), hi);
+                tmem_st16_async(la + S_LO + (uint32_t)(k0 >> 1), lo);
+                tmem_st32_async(la + S_ACC + (uint32_t)k0, sc);
+            }
+            tmem_wait_st();
         }
-        if (warp == 0 && c + 1 < NC) inter_issue_B(sm, R + (size_t)vc * REC, lane);
-        __syncthreads();
+        fence_before_sync();
+        mbar_arrive(&sm.s_ready);
+        for (int c = 0; c < NC && ok; ++c) {
+            const uint32_t ph = (uint32_t)(c & 1);
+            // U^T = U0^T - S W^T  -> bf16 pairs (columns t in [32h, 32h + 32))
+            if (!wait_or_flag(&sm.mma1_done, ph, err, ok) || !wait_or_flag(&sm.full_u0, ph, err, ok)) break;
+            fence_after_sync();
+            {
+                float x[32];
+                tmem_ld32(la + D_U + 32u * h, x);
+                uint32_t hi[16], lo[16];
+                const unsigned char* u0 = sm.u0t + (uint32_t)h * 16384u;
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 a = *reinterpret_cast<const float4*>(u0 + sw128_off_b32((uint32_t)v, 4u * j4));
+                    split2_bf16(a.x - x[4 * j4], a.y - x[4 * j4 + 1], hi[2 * j4], lo[2 * j4]);
+                    split2_bf16(a.z - x[4 * j4 + 2], a.w - x[4 * j4 + 3], hi[2 * j4 + 1], lo[2 * j4 + 1]);
+                }
+                tmem_st16_async(la + U_HI + 16u * h, hi);
+                tmem_st16_async(la + U_LO + 16u * h, lo);
+                tmem_wait_st();
+            }
+            fence_before_sync();
+            mbar_arrive(&sm.u_ready);
+            // S epilogue: S_{c+1} -> S_HI/S_LO and S_ACC <- e^{G_last(c+1)} S_{c+1}; or the final state
+            if (!wait_or_flag(&sm.mma3_done, ph, err, ok)) break;
+            fence_after_sync();
+            const bool last = c + 1 == NC;
+            float e1 = 1.0f;
+            if (!last) {
+                const int s = (c + 1) & 3;
+                if (!wait_or_flag(&sm.full_g[s], (uint32_t)(((c + 1) >> 2) & 1), err, ok)) break;
+                e1 = expf(sm.gring[s][C - 1]);
+            }
+            for (int piece = 0; piece < 2; ++piece) {
+                const int k0 = 64 * h + 32 * piece;
+                uint32_t r[32];
+                tmem_ld32_async(la + S_ACC + (uint32_t)k0, r);
+                tmem_wait_ld();
+                if (last) {
+#pragma unroll
+                    for (int j4 = 0; j4 < 8; ++j4)
+                        *reinterpret_cast<float4*>(Sg + k0 + 4 * j4) =
+                            make_float4(__uint_as_float(r[4 * j4]), __uint_as_float(r[4 * j4 + 1]),
+                                        __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3]));
+                } else {
+                    uint32_t hi[16], lo[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        split2_bf16(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]), hi[j], lo[j]);
+                    tmem_st16_async(la + S_HI + (uint32_t)(k0 >> 1), hi);
+                    tmem_st16_async(la + S_LO + (uint32_t)(k0 >> 1), lo);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * e1);
+                    tmem_st32_async(la + S_ACC + (uint32_t)k0, r);
+                }
+            }
+            if (!last) {
+                tmem_wait_st();
+                fence_before_sync();
+                mbar_arrive(&sm.s_ready);
+            }
+        }
+    } else if (warp >= ES_W0) {
+        // ---------------- Q e^G and K e^{G_last - G} ----------------
+        const int et = tid - ES_W0 * 32;
+        for (int c = 0; c < NC && ok; ++c) {
+            const uint32_t ph = (uint32_t)(c & 1);
+            const int s = c & 3;
+            if (!wait_or_flag(&sm.full_g[s], (uint32_t)((c >> 2) & 1), err, ok)) break;
+            const float* G = sm.gring[s];
+            if (!wait_or_flag(&sm.full_q, ph, err, ok)) break;
+            scale_rows(sm.qe, sm.qe, et, 128, [&](int t) { return expf(G[t]); });
+            fence_proxy_async_smem();
+            mbar_arrive(&sm.qe_ready);
+            if (!wait_or_flag(&sm.full_k, ph, err, ok)) break;
+            if (c > 0 && !wait_or_flag(&sm.mma3_done, (uint32_t)((c - 1) & 1), err, ok)) break;
+            const float Gl = G[C - 1];
+            scale_rows(sm.kraw, sm.kd, et, 128, [&](int t) { return expf(Gl - G[t]); });
+            fence_proxy_async_smem();
+            mbar_arrive(&sm.kd_ready);
+        }
+    } else {
+        // ---------------- y epilogue: gated RMSNorm of Y^T, thread = v ----------------
+        const int ew = warp - EY_W0;
+        const int v = 32 * ew + lane;
+        const uint32_t la = tmem + ((uint32_t)(32 * ew) << 16);
+        const float wv = norm_w[v];
+        float* yb = y_out + (size_t)vl * D + v;
+        for (int c = 0; c < NC; ++c) {
+            const bool got = ok && wait_or_flag(&sm.mma2_done[c & 1], (uint32_t)((c >> 1) & 1), err, ok);
+            if (!named_bar_and(1, 128, got)) {
+                ok = false;
+                break;
+            }
+            fence_after_sync();
+            float y[C];
+            {
+                uint32_t r[32];
+                const uint32_t dy = D_Y + 64u * (uint32_t)(c & 1);
+                tmem_ld32_async(la + dy, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) y[j] = __uint_as_float(r[j]);
+                tmem_ld32_async(la + dy + 32u, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) y[32 + j] = __uint_as_float(r[j]);
+            }
+            fence_before_sync();
+            mbar_arrive(&sm.y_free[c & 1]);
+            // sum over this warp's 32 v of y^2 for each of the 64 tokens: halving butterfly,
+            // lane L ends with tokens 2L and 2L+1
+            float a[C];
+#pragma unroll
+            for (int j = 0; j < C; ++j) a[j] = y[j] * y[j];
+            bfly_reduce<64, 16>(a, lane);
+            bfly_reduce<32, 8>(a, lane);
+            bfly_reduce<16, 4>(a, lane);
+            bfly_reduce<8, 2>(a, lane);
+            bfly_reduce<4, 1>(a, lane);
+            sm.red[ew][2 * lane] = a[0];
+            sm.red[ew][2 * lane + 1] = a[1];
+            tc::named_bar_sync(1, 128);
+            if (ew < 2) {
+                const int t = 32 * ew + lane;
+                const float ss = (sm.red[0][t] + sm.red[1][t]) + (sm.red[2][t] + sm.red[3][t]);
+                sm.inv[t] = 1.0f / sqrtf(ss / (float)D + 1e-6f);
+            }
+            tc::named_bar_sync(1, 128);
+            const bool zok = wait_or_flag(&sm.full_z, (uint32_t)(c & 1), err, ok);
+            const int64_t t0 = (int64_t)c * C;
+            const int n = (int)(T - t0 < C ? T - t0 : C);
+            if (zok) {
+#pragma unroll
+                for (int t = 0; t < C; ++t)
+                    if (t < n)
+                        yb[(size_t)(t0 + t) * vc * D] = ((y[t] * sm.inv[t]) * wv) * siluf_acc(sm.zt[t][v]);
+            }
+            mbar_arrive(&sm.z_free);
+        }
     }
-    if (!ok) return;
-    for (int i = tid; i < VB * (D / 4); i += 128) {
-        const int r = i / (D / 4), c4 = i % (D / 4);
-        reinterpret_cast<float4*>(Sg + (size_t)r * D)[c4] = *reinterpret_cast<const float4*>(&sm.S[r][4 * c4]);
-    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == CTL_W) tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
-// gated RMSNorm (prefill variant, ss / head_dim; ssm.rs:294-334), per token
+// host side
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) gdn_pf_gate_kernel(int vh0, int vc, const float* __restrict__ yraw,
-                                                          const float* __restrict__ z,
-                                                          const float* __restrict__ norm_w,
-                                                          float* __restrict__ y_out) {
-    const int64_t t = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float4 w = reinterpret_cast<const float4*>(norm_w)[lane];
-    for (int vl = warp; vl < vc; vl += 8) {
-        const float4 y = reinterpret_cast<const float4*>(yraw + ((size_t)t * vc + vl) * SSM_D)[lane];
-        const float ss = warp_sum(y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w);
-        const float inv = 1.0f / sqrtf(ss / (float)SSM_D + 1e-6f);
-        const float4 zz = reinterpret_cast<const float4*>(z + (size_t)t * INNER + (size_t)(vh0 + vl) * SSM_D)[lane];
-        float4 o;
-        o.x = ((y.x * inv) * w.x) * siluf_acc(zz.x);
-        o.y = ((y.y * inv) * w.y) * siluf_acc(zz.y);
-        o.z = ((y.z * inv) * w.z) * siluf_acc(zz.z);
-        o.w = ((y.w * inv) * w.w) * siluf_acc(zz.w);
-        reinterpret_cast<float4*>(y_out + ((size_t)t * vc + vl) * SSM_D)[lane] = o;
-    }
+namespace {
+// bf16 [heads][2][Tp][128] (hi | lo rows) with (64 x 64 x 1 x 1) boxes, 128-byte swizzle
+bool make_split_map(CUtensorMap* m, const void* base, int64_t Tp, int heads) {
+    EncodeTiledFn fn = tensor_map_encoder();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)SSM_D, (cuuint64_t)Tp, 2, (cuuint64_t)heads};
+    cuuint64_t strides[3] = {(cuuint64_t)SSM_D * 2, (cuuint64_t)Tp * SSM_D * 2, (cuuint64_t)2 * Tp * SSM_D * 2};
+    cuuint32_t box[4] = {64, 64, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+// z [T][6144] f32 with (128 x 64) boxes, no swizzle; rows past T read as zero
+bool make_z_map(CUtensorMap* m, const float* z, int64_t T) {
+    EncodeTiledFn fn = tensor_map_encoder();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)INNER, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)INNER * 4};
+    cuuint32_t box[2] = {(cuuint32_t)SSM_D, (cuuint32_t)gp::C};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(z), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+}  // namespace
 
 cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* qkv, const float* alpha,
                                const float* beta, const float* z, float* y, cudaStream_t st, int* n_launch) {
@@ -560,29 +852,40 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
     const SsmSlot slot = L.h_ssm[seq];
     const int h0 = L.head[seq];
     const int NC = (int)((T + C - 1) / C);
-    const size_t n_qk = (size_t)T * SSM_HK * D, n_v = (size_t)T * vc * D, n_g = (size_t)T * vc;
-    const size_t n_rec = (size_t)NC * vc * REC;
-    const size_t total = 2 * n_qk + 2 * n_v + 2 * n_g + n_rec + 64;
-    cudaError_t e = ensure_prefill_scratch(ctx, total * sizeof(float));
+    const int64_t Tp = (int64_t)NC * C;
+    // scratch: q/k/v operand rows, gates, records
+    const size_t qk_bytes = round_up((size_t)SSM_HK * 2 * Tp * D * 2, 1024);
+    const size_t v_bytes = round_up((size_t)vc * 2 * Tp * D * 2, 1024);
+    const size_t g_bytes = round_up((size_t)vc * Tp * 4, 1024);
+    const size_t rec_bytes = (size_t)NC * vc * REC_BYTES;
+    cudaError_t e = ensure_prefill_scratch(ctx, 2 * qk_bytes + v_bytes + 2 * g_bytes + rec_bytes + 1024);
     if (e != cudaSuccess) return e;
-    float* qn = static_cast<float*>(ctx->pf);
-    float* kn = qn + n_qk;
-    float* vv = kn + n_qk;
-    float* yraw = vv + n_v;
-    float* gl = yraw + n_v;
-    float* bt = gl + n_g;
-    float* rec = bt + n_g;
-    rec = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(rec) + 15) & ~uintptr_t(15));
+    unsigned char* base = reinterpret_cast<unsigned char*>(round_up(reinterpret_cast<uintptr_t>(ctx->pf), 1024));
+    __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(base);
+    __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(base + qk_bytes);
+    __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(base + 2 * qk_bytes);
+    float* gl = reinterpret_cast<float*>(base + 2 * qk_bytes + v_bytes);
+    float* bt = reinterpret_cast<float*>(base + 2 * qk_bytes + v_bytes + g_bytes);
+    unsigned char* rec = base + 2 * qk_bytes + v_bytes + 2 * g_bytes;
 
-    gdn_pf_conv_kernel<<<(unsigned)T, 256, 0, st>>>(T, vh0, vc, h0, qkv, slot.hist, L.conv_w, L.ssm_a, L.dt_bias,
-                                                    alpha, beta, qn, kn, vv, gl, bt);
+    CUtensorMap mq, mk, mv, mz;
+    if (!make_split_map(&mq, qs, Tp, SSM_HK) || !make_split_map(&mk, ks, Tp, SSM_HK) ||
+        !make_split_map(&mv, vs, Tp, vc) || !make_z_map(&mz, z, T))
+        return cudaErrorInvalidValue;
+
+    gdn_pf_prep_kernel<<<(unsigned)Tp, 256, 0, st>>>(T, Tp, vh0, vc, h0, qkv, slot.hist, L.conv_w, L.ssm_a,
+                                                     L.dt_bias, alpha, beta, qs, ks, vs, gl, bt);
     gdn_pf_ring_kernel<<<(unsigned)(T < CONV_K ? T : CONV_K), 256, 0, st>>>(T, h0, qkv, slot.hist);
-    cudaFuncSetAttribute(gdn_pf_intra_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(IntraSmem));
-    gdn_pf_intra_kernel<<<dim3(NC, vc), 256, sizeof(IntraSmem), st>>>(T, vh0, vc, qn, kn, vv, gl, bt, rec);
-    cudaFuncSetAttribute(gdn_pf_inter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(InterSmem));
-    gdn_pf_inter_kernel<<<dim3(D / VB, vc), 128, sizeof(InterSmem), st>>>(T, vc, rec, slot.state, yraw, ctx->d_err);
-    gdn_pf_gate_kernel<<<(unsigned)T, 256, 0, st>>>(vh0, vc, yraw, z, L.norm_w, y);
-    *n_launch += 5;
+    const int smem_i = (int)sizeof(IntraSmem) + 1024;
+    e = cudaFuncSetAttribute(gdn_pf_intra_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_i);
+    if (e != cudaSuccess) return e;
+    gdn_pf_intra_kernel<<<dim3(NC, vc), 256, smem_i, st>>>(mq, mk, mv, Tp, vh0, vc, gl, bt, rec, ctx->d_err);
+    const int smem_c = (int)sizeof(ChainSmem) + 1024;
+    e = cudaFuncSetAttribute(gdn_pf_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_c);
+    if (e != cudaSuccess) return e;
+    gdn_pf_chain_kernel<<<vc, CHAIN_THREADS, smem_c, st>>>(mq, mk, mz, T, NC, vh0, vc, rec, slot.state, L.norm_w, y,
+                                                           ctx->d_err);
+    *n_launch += 4;
     return cudaGetLastError();
 }
 
