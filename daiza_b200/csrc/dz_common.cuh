@@ -48,13 +48,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// try_wait suspends the thread in hardware until the phase completes or the
+// hint (ns) runs out, so waiting warps do not spin on the issue slots that the
+// working warps of the same sub-partition need.
+constexpr uint32_t MBAR_SUSPEND_HINT_NS = 100000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(MBAR_SUSPEND_HINT_NS) : "memory");
     return ok != 0;
 }
 
@@ -65,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 0 && global_ns() - t0 > MBAR_WAIT_LIMIT_NS) break;
+        if ((i & 15u) == 0 && global_ns() - t0 > MBAR_WAIT_LIMIT_NS) break;
     }
     if (err) atomicExch(err, DEVERR_MBAR_TIMEOUT);
     return false;

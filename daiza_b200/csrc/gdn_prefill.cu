@@ -36,6 +36,7 @@
 //                 prefill; per chunk  U^T = U0^T - S W^T,  Y^T = S Qe^T + U^T P^T,
 //                 S = e^{G_last} S + U^T Kd, with warp-specialised loader, MMA
 //                 issuer and epilogues; the gated RMSNorm output is fused.
+#include <algorithm>
 #include <cstddef>
 
 #include "dz_internal.h"
@@ -142,24 +143,29 @@ __device__ __forceinline__ S& align1024(unsigned char* raw) {
 }
 
 // ---------------------------------------------------------------------------
-// intra-chunk WY transform: one CTA (8 warps) per (chunk, local v head)
+// intra-chunk WY transform: persistent CTAs (8 warps) over the (chunk, local v
+// head) items in chunk-major order.  K and Q of the next item are loaded while
+// the current one is processed; V goes into the current item's Q rows once
+// [K;Q] K^T is done.
 // ---------------------------------------------------------------------------
 namespace gp {
-constexpr int TP = C + 4;        // padded f32 row for the 64x64 triangular solve
+constexpr int TP = C + 1;        // padded f32 row of the 64x64 matrices (conflict-free column access)
 struct alignas(1024) IntraSmem {
-    // [hi|lo][d-box][row][64]: rows 0-63 = K of the chunk, 64-127 = Q.  After the
-    // W / U0 products this 64 KB holds the W images (32 KB) then the U0^T image.
-    __nv_bfloat16 kq[2][2][128][64];
-    __nv_bfloat16 v[2][2][64][64];    // [hi|lo][d-box][s][64]
-    __nv_bfloat16 tmw[2][64][64];     // Tm diag(beta e^G), [hi|lo][t][s] K-major
-    __nv_bfloat16 tmb[2][64][64];     // Tm diag(beta)
-    __nv_bfloat16 p[2][64][64];       // P image [hi|lo][t][s]
-    float am[C][TP];                  // strictly lower beta_t Gam_ts k_t.k_s
+    // per buffer: [hi|lo][d-box][row][64]; rows 0-63 = K of the item, 64-127 = Q,
+    // then V.  After the W / U0 products a buffer holds the W images (32 KB) then
+    // the U0^T image (32 KB) until their bulk store has read them.
+    __nv_bfloat16 kq[2][2][2][128][64];
+    // A (f32 [64][TP]) and, at U_P, the P image (16 KB), then the block scratch of
+    // the inverse; after the inverse: Tm diag(beta e^G) and Tm diag(beta) split
+    // images [hi|lo][t][s] (8 KB each) at 0 and 16 KB
+    unsigned char u[17408 + 16384];
     float tm[C][TP];                  // (I + A)^-1
-    float g[C], b[C], G[C], eG[C];
-    uint64_t bar_in, bar_m1, bar_m2;
+    float g[2][C], b[2][C], G[C], eG[C];
+    uint64_t bar_kq[2], bar_v, bar_m1, bar_m2;
     uint32_t tmem_base;
 };
+constexpr uint32_t U_P = 17408;
+static_assert(C * TP * 4 <= U_P, "A ends before the P image");
 // TMEM columns of the intra kernel
 constexpr uint32_t I_KQ = 0, I_W = 64, I_U0 = 128;
 }  // namespace gp
@@ -167,21 +173,26 @@ constexpr uint32_t I_KQ = 0, I_W = 64, I_U0 = 128;
 __global__ void __launch_bounds__(256, 1) gdn_pf_intra_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                               const __grid_constant__ CUtensorMap tm_k,
                                                               const __grid_constant__ CUtensorMap tm_v, int64_t Tp,
-                                                              int vh0, int vc, const float* __restrict__ gl,
+                                                              int n_items, int vh0, int vc,
+                                                              const float* __restrict__ gl,
                                                               const float* __restrict__ bt,
                                                               unsigned char* __restrict__ rec, int* err) {
     using namespace gp;
     using namespace tc;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     IntraSmem& sm = align1024<IntraSmem>(smem_raw);
-    const int c = blockIdx.x, vl = blockIdx.y, tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31;
-    const int kh = (vh0 + vl) % SSM_HK;
-    const int t0 = c * C;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float (*am)[TP] = reinterpret_cast<float (*)[TP]>(sm.u);
+    unsigned char* pimg = sm.u + U_P;
+    float* xs = reinterpret_cast<float*>(sm.u + U_P);     // block scratch (after the P image is stored)
+    unsigned char* tmw = sm.u;                               // [hi|lo][64][64] bf16 (after the inverse)
+    unsigned char* tmb = sm.u + 16384;
 
     if (warp == 0) tmem_alloc(&sm.tmem_base, 256);
     if (tid == 0) {
-        mbar_init(&sm.bar_in, 1);
+        mbar_init(&sm.bar_kq[0], 1);
+        mbar_init(&sm.bar_kq[1], 1);
+        mbar_init(&sm.bar_v, 1);
         mbar_init(&sm.bar_m1, 1);
         mbar_init(&sm.bar_m2, 1);
         fence_mbar_init();
@@ -192,224 +203,284 @@ __global__ void __launch_bounds__(256, 1) gdn_pf_intra_kernel(const __grid_const
     const uint32_t tmem = sm.tmem_base;
     bool ok = true;
 
-    if (tid == 0) {
-        mbar_arrive_expect_tx(&sm.bar_in, 12 * 8192 + 2 * 256);
+    // K, Q, g, beta of item i into buffer b
+    auto load_kq = [&](int i, int b) {
+        const int c = i / vc, vl = i % vc, kh = (vh0 + vl) % SSM_HK, t0 = c * C;
+        mbar_arrive_expect_tx(&sm.bar_kq[b], 8 * 8192 + 2 * 256);
         for (int hl = 0; hl < 2; ++hl)
             for (int db = 0; db < 2; ++db) {
-                tma_load_4d(&sm.kq[hl][db][0][0], &tm_k, 64 * db, t0, hl, kh, &sm.bar_in);
-                tma_load_4d(&sm.kq[hl][db][64][0], &tm_q, 64 * db, t0, hl, kh, &sm.bar_in);
-                tma_load_4d(&sm.v[hl][db][0][0], &tm_v, 64 * db, t0, hl, vl, &sm.bar_in);
+                tma_load_4d(&sm.kq[b][hl][db][0][0], &tm_k, 64 * db, t0, hl, kh, &sm.bar_kq[b]);
+                tma_load_4d(&sm.kq[b][hl][db][64][0], &tm_q, 64 * db, t0, hl, kh, &sm.bar_kq[b]);
             }
-        bulk_g2s(sm.g, gl + (size_t)vl * Tp + t0, 256, &sm.bar_in);
-        bulk_g2s(sm.b, bt + (size_t)vl * Tp + t0, 256, &sm.bar_in);
-    }
-    wait_or_flag(&sm.bar_in, 0, err, ok);
+        bulk_g2s(sm.g[b], gl + (size_t)vl * Tp + t0, 256, &sm.bar_kq[b]);
+        bulk_g2s(sm.b[b], bt + (size_t)vl * Tp + t0, 256, &sm.bar_kq[b]);
+    };
+    if (tid == 0 && (int)blockIdx.x < n_items) load_kq(blockIdx.x, 0);
 
-    // ---- [K; Q] K^T  (M 128, N 64, K 128; three split products)
-    if (tid == 0 && ok) {
-        fence_after_sync();
-        constexpr uint32_t ID = idesc_bf16(128, 64, false);
-        const uint32_t kq_hi = smem_u32(&sm.kq[0][0][0][0]), kq_lo = smem_u32(&sm.kq[1][0][0][0]);
-        uint32_t acc = 0;
-        for (int pass = 0; pass < 3; ++pass) {
-            const uint32_t a = pass == 2 ? kq_lo : kq_hi, b = pass == 1 ? kq_lo : kq_hi;
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t off = (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u;
-                umma_ss(tmem + I_KQ, sw128_desc(a + off, 16, 1024), sw128_desc(b + off, 16, 1024), ID, acc);
-                acc = 1;
-            }
-        }
-        umma_commit(&sm.bar_m1);
-    }
-    if (warp == 1) {   // inclusive cumsum of the 64 log decays (2 per lane)
-        const float a0 = sm.g[2 * lane], a1 = sm.g[2 * lane + 1];
-        float s = a0 + a1;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, s, o);
-            if (lane >= o) s += y;
-        }
-        const float excl = s - (a0 + a1);
-        sm.G[2 * lane] = excl + a0;
-        sm.G[2 * lane + 1] = excl + a0 + a1;
-        sm.eG[2 * lane] = expf(excl + a0);
-        sm.eG[2 * lane + 1] = expf(excl + a0 + a1);
-    }
-    __syncthreads();
-
-    // ---- epilogue 1: rows 0-63 -> A (f32, for the solve), rows 64-127 -> P image
     const int q4 = warp & 3, h = warp >> 2;
     const int row = 32 * q4 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
-    if (wait_or_flag(&sm.bar_m1, 0, err, ok)) {
-        fence_after_sync();
-        float x[32];
-        tmem_ld32(lane_addr + I_KQ + 32 * h, x);
-        if (row < C) {
-            const int t = row;
-            const float bt_ = sm.b[t], Gt = sm.G[t];
+    int n = 0;
+    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++n) {
+        const int buf = n & 1;
+        const int c = i / vc, vl = i % vc, kh = (vh0 + vl) % SSM_HK;
+        unsigned char* R = rec + ((size_t)c * vc + vl) * REC_BYTES;
+        const uint32_t ph = (uint32_t)(n & 1);
+        if (tid == 0) {
+            bulk_wait_read_all();              // every store of item n-1 (other buffer, P, G) has read smem
+            if (i + (int)gridDim.x < n_items) load_kq(i + gridDim.x, buf ^ 1);
+        }
+        wait_or_flag(&sm.bar_kq[buf], (uint32_t)((n >> 1) & 1), err, ok);
+        if (!__syncthreads_and(ok)) break;     // every thread takes the same path
+        const uint32_t kq_hi = smem_u32(&sm.kq[buf][0][0][0][0]), kq_lo = smem_u32(&sm.kq[buf][1][0][0][0]);
+        // ---- [K; Q] K^T  (M 128, N 64, K 128; three split products)
+        if (tid == 0) {
+            fence_after_sync();
+            constexpr uint32_t ID = idesc_bf16(128, 64, false);
+            const uint64_t dh = sw128_desc(kq_hi, 16, 1024), dl = sw128_desc(kq_lo, 16, 1024);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int s = 32 * h + j;
-                sm.am[t][s] = s < t ? bt_ * expf(Gt - sm.G[s]) * x[j] : 0.0f;
+            for (int pass = 0; pass < 3; ++pass) {
+                const uint64_t a = pass == 2 ? dl : dh, bb = pass == 1 ? dl : dh;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint64_t off = (uint64_t)(((ks >> 2) * 16384 + (ks & 3) * 32) >> 4);
+                    umma_ss(tmem + I_KQ, a + off, bb + off, ID, (pass | ks) != 0);
+                }
+            }
+            umma_commit(&sm.bar_m1);
+        }
+        if (warp == 1) {   // inclusive cumsum of the 64 log decays (2 per lane)
+            const float a0 = sm.g[buf][2 * lane], a1 = sm.g[buf][2 * lane + 1];
+            float sum = a0 + a1;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_up_sync(0xffffffffu, sum, o);
+                if (lane >= o) sum += y;
+            }
+            const float excl = sum - (a0 + a1);
+            sm.G[2 * lane] = excl + a0;
+            sm.G[2 * lane + 1] = excl + a0 + a1;
+            sm.eG[2 * lane] = expf(excl + a0);
+            sm.eG[2 * lane + 1] = expf(excl + a0 + a1);
+        }
+        wait_or_flag(&sm.bar_m1, ph, err, ok);
+        if (!__syncthreads_and(ok)) break;
+        fence_after_sync();
+        if (tid == 0) {   // V into the Q rows (Q is no longer read)
+            mbar_arrive_expect_tx(&sm.bar_v, 4 * 8192);
+            for (int hl = 0; hl < 2; ++hl)
+                for (int db = 0; db < 2; ++db)
+                    tma_load_4d(&sm.kq[buf][hl][db][64][0], &tm_v, 64 * db, c * C, hl, vl, &sm.bar_v);
+        }
+        // ---- epilogue 1: rows 0-63 -> A (f32, for the inverse), rows 64-127 -> P image
+        const float* bcur = sm.b[buf];
+        {
+            float x[32];
+            tmem_ld32(lane_addr + I_KQ + 32 * h, x);
+            if (row < C) {
+                const int t = row;
+                const float bt_ = bcur[t], Gt = sm.G[t];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int s = 32 * h + j;
+                    am[t][s] = s < t ? bt_ * __expf(Gt - sm.G[s]) * x[j] : 0.0f;
+                }
+            } else {
+                const int t = row - C;
+                const float Gt = sm.G[t];
+#pragma unroll
+                for (int j8 = 0; j8 < 4; ++j8) {
+                    uint4 hi, lo;
+                    uint32_t* hp = &hi.x;
+                    uint32_t* lp = &lo.x;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int j = 8 * j8 + 2 * e, s = 32 * h + j;
+                        const float p0 = s <= t ? __expf(Gt - sm.G[s]) * x[j] : 0.0f;
+                        const float p1 = s + 1 <= t ? __expf(Gt - sm.G[s + 1]) * x[j + 1] : 0.0f;
+                        split2_bf16(p0, p1, hp[e], lp[e]);
+                    }
+                    const uint32_t off = sw128_off_b16((uint32_t)t, (uint32_t)(32 * h + 8 * j8));
+                    *reinterpret_cast<uint4*>(pimg + off) = hi;
+                    *reinterpret_cast<uint4*>(pimg + 8192 + off) = lo;
+                }
+            }
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            bulk_s2g(R + REC_P, pimg, 16384);
+            bulk_s2g(R + REC_G, sm.G, 256);
+            bulk_commit();
+        }
+        // ---- Tm = (I + A)^-1.  Level 1: the four 16x16 diagonal blocks, lane j = column j
+        if (warp < 4) {
+            if (lane < 16) {
+                const int b0 = 16 * warp, j = lane;
+                float x[16];
+#pragma unroll
+                for (int r = 0; r < 16; ++r) {
+                    float acc = r == j ? 1.0f : 0.0f;
+#pragma unroll
+                    for (int q = 0; q < r; ++q) acc = fmaf(-am[b0 + r][b0 + q], x[q], acc);
+                    x[r] = acc;
+                }
+#pragma unroll
+                for (int r = 0; r < 16; ++r) sm.tm[b0 + r][b0 + j] = x[r];
             }
         } else {
-            const int t = row - C;
-            const float Gt = sm.G[t];
-#pragma unroll
-            for (int j8 = 0; j8 < 4; ++j8) {
-                uint4 hi, lo;
-                uint32_t* hp = &hi.x;
-                uint32_t* lp = &lo.x;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int j = 8 * j8 + 2 * e, s = 32 * h + j;
-                    const float p0 = s <= t ? expf(Gt - sm.G[s]) * x[j] : 0.0f;
-                    const float p1 = s + 1 <= t ? expf(Gt - sm.G[s + 1]) * x[j + 1] : 0.0f;
-                    split2_bf16(p0, p1, hp[e], lp[e]);
-                }
-                const uint32_t off = sw128_off_b16((uint32_t)t, (uint32_t)(32 * h + 8 * j8));
-                *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.p[0][0][0]) + off) = hi;
-                *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.p[1][0][0]) + off) = lo;
+            // zero the strictly upper blocks (block row I < block column J)
+            for (int e = tid - 128; e < 6 * 256; e += 128) {
+                const int blk = e >> 8, w = e & 255;
+                const int I = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+                const int J = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+                sm.tm[16 * I + (w >> 4)][16 * J + (w & 15)] = 0.0f;
             }
         }
-    }
-    __syncthreads();
-
-    // ---- Tm = (I + A)^-1, blocked 16x16.  Diagonal blocks: warp b, forward substitution.
-    if (warp < 4) {
-        const int b0 = 16 * warp;
-        for (int i = 0; i < 16; ++i) {
-            if (lane < 16) {
-                const int j = lane;
-                float xv = (i == j) ? 1.0f : 0.0f;
-                for (int s = j; s < i; ++s) xv = fmaf(-sm.am[b0 + i][b0 + s], sm.tm[b0 + s][b0 + j], xv);
-                sm.tm[b0 + i][b0 + j] = (j <= i) ? xv : 0.0f;
-                for (int jj = b0 + 16; jj < C; jj += 16) sm.tm[b0 + i][jj + j] = 0.0f;   // strictly upper blocks
+        if (tid == 0) bulk_wait_read_all();   // the P image is read: its bytes become scratch
+        __syncthreads();
+        // Level 2: T_10 = -T_11 (A_10 T_00) and T_32 = -T_33 (A_32 T_22); two outputs a thread
+        {
+            const int pr = tid >> 7, idx = tid & 127;
+            const int I = 1 + 2 * pr, J = 2 * pr;
+            const int r = idx >> 3, c0 = (idx & 7) * 2;
+            float* X = xs + pr * 16 * 17;
+            float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                const float av = am[16 * I + r][16 * J + q];
+                a0 = fmaf(av, sm.tm[16 * J + q][16 * J + c0], a0);
+                a1 = fmaf(av, sm.tm[16 * J + q][16 * J + c0 + 1], a1);
             }
-            __syncwarp();
-        }
-    }
-    __syncthreads();
-    // off-diagonal blocks by block diagonal d: T_IJ = -T_II * sum_{K=J}^{I-1} A_IK T_KJ
-    for (int d = 1; d < 4; ++d) {
-        if (warp < 4 - d) {
-            const int J = warp, I = warp + d;
-            const int r = lane >> 1, cb = 8 * (lane & 1);
-            float m[8];
+            X[r * 17 + c0] = a0;
+            X[r * 17 + c0 + 1] = a1;
+            __syncthreads();
+            float t0v = 0.0f, t1v = 0.0f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) m[e] = 0.0f;
-            for (int Kb = J; Kb < I; ++Kb)
-                for (int s = 0; s < 16; ++s) {
-                    const float a = sm.am[16 * I + r][16 * Kb + s];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) m[e] = fmaf(a, sm.tm[16 * Kb + s][16 * J + cb + e], m[e]);
-                }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) sm.tm[16 * I + r][16 * J + cb + e] = m[e];
-            __syncwarp();
-            float o[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = 0.0f;
-            for (int s = 0; s <= r; ++s) {
-                const float tii = sm.tm[16 * I + r][16 * I + s];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) o[e] = fmaf(tii, sm.tm[16 * I + s][16 * J + cb + e], o[e]);
+            for (int q = 0; q < 16; ++q) {
+                const float tv = sm.tm[16 * I + r][16 * I + q];
+                t0v = fmaf(tv, X[q * 17 + c0], t0v);
+                t1v = fmaf(tv, X[q * 17 + c0 + 1], t1v);
             }
-            __syncwarp();
-#pragma unroll
-            for (int e = 0; e < 8; ++e) sm.tm[16 * I + r][16 * J + cb + e] = -o[e];
+            sm.tm[16 * I + r][16 * J + c0] = -t0v;
+            sm.tm[16 * I + r][16 * J + c0 + 1] = -t1v;
         }
         __syncthreads();
-    }
-    // ---- Tm diag(beta e^G) and Tm diag(beta) as split K-major images [t][s]
-    for (int i = tid; i < C * 8; i += 256) {
-        const int t = i >> 3, j8 = i & 7;
-        uint4 wh, wl, bh, bl;
-        uint32_t *whp = &wh.x, *wlp = &wl.x, *bhp = &bh.x, *blp = &bl.x;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int s = 8 * j8 + 2 * e;
-            const float a0 = sm.tm[t][s], a1 = sm.tm[t][s + 1];
-            const float cb0 = sm.b[s], cb1 = sm.b[s + 1];
-            split2_bf16(a0 * cb0 * sm.eG[s], a1 * cb1 * sm.eG[s + 1], whp[e], wlp[e]);
-            split2_bf16(a0 * cb0, a1 * cb1, bhp[e], blp[e]);
-        }
-        const uint32_t off = sw128_off_b16((uint32_t)t, (uint32_t)(8 * j8));
-        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.tmw[0][0][0]) + off) = wh;
-        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.tmw[1][0][0]) + off) = wl;
-        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.tmb[0][0][0]) + off) = bh;
-        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&sm.tmb[1][0][0]) + off) = bl;
-    }
-    fence_proxy_async_smem();
-    __syncthreads();
-
-    // ---- W^T = K^T TmW^T and U0^T = V^T TmB^T  (M 128 over k / v, N 64, K 64; A MN-major)
-    if (tid == 0 && ok) {
-        fence_after_sync();
-        constexpr uint32_t ID = idesc_bf16(128, 64, false, true);
-        const uint32_t k_hi = smem_u32(&sm.kq[0][0][0][0]), k_lo = smem_u32(&sm.kq[1][0][0][0]);
-        const uint32_t v_hi = smem_u32(&sm.v[0][0][0][0]), v_lo = smem_u32(&sm.v[1][0][0][0]);
-        const uint32_t w_hi = smem_u32(&sm.tmw[0][0][0]), w_lo = smem_u32(&sm.tmw[1][0][0]);
-        const uint32_t b_hi = smem_u32(&sm.tmb[0][0][0]), b_lo = smem_u32(&sm.tmb[1][0][0]);
-        uint32_t acc = 0;
-        for (int pass = 0; pass < 3; ++pass) {
-            const uint32_t a = pass == 2 ? k_lo : k_hi, b = pass == 1 ? w_lo : w_hi;
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                // A: K rows s (128 B of d each), d blocks of 64 in the 16 KB d-boxes
-                umma_ss(tmem + I_W, sw128_desc(a + (uint32_t)ks * 2048u, 16384, 1024),
-                        sw128_desc(b + (uint32_t)ks * 32u, 16, 1024), ID, acc);
-                acc = 1;
-            }
-        }
-        acc = 0;
-        for (int pass = 0; pass < 3; ++pass) {
-            const uint32_t a = pass == 2 ? v_lo : v_hi, b = pass == 1 ? b_lo : b_hi;
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                umma_ss(tmem + I_U0, sw128_desc(a + (uint32_t)ks * 2048u, 8192, 1024),
-                        sw128_desc(b + (uint32_t)ks * 32u, 16, 1024), ID, acc);
-                acc = 1;
-            }
-        }
-        umma_commit(&sm.bar_m2);
-    }
-    unsigned char* img = reinterpret_cast<unsigned char*>(&sm.kq[0][0][0][0]);   // W images, then U0^T image
-    if (wait_or_flag(&sm.bar_m2, 0, err, ok)) {
-        fence_after_sync();
-        float x[32];
-        // W^T: lane = k, columns t in [32h, 32h + 32) -> W[t][k] images
-        tmem_ld32(lane_addr + I_W + 32 * h, x);
+        // Level 3: T_21 (rows 32-63, cols 0-31) = -T_2 (A_21 T_1); four outputs a thread
         {
-            const uint32_t kb = (uint32_t)row >> 6, kc = (uint32_t)row & 63u;
+            const int r = tid >> 3, c0 = (tid & 7) * 4;
+            float* X = xs;                     // [32][33]
+            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+            for (int q = 0; q < 32; ++q) {
+                const float av = am[32 + r][q];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) a[e] = fmaf(av, sm.tm[q][c0 + e], a[e]);
+            }
+            __syncthreads();                   // every level-2 read of xs is done
+#pragma unroll
+            for (int e = 0; e < 4; ++e) X[r * 33 + c0 + e] = a[e];
+            __syncthreads();
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a[e] = 0.0f;
+#pragma unroll 8
+            for (int q = 0; q < 32; ++q) {
+                const float tv = sm.tm[32 + r][32 + q];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) a[e] = fmaf(tv, X[q * 33 + c0 + e], a[e]);
+            }
+            __syncthreads();                   // A and the scratch are no longer read
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sm.tm[32 + r][c0 + e] = -a[e];
+        }
+        __syncthreads();
+        // ---- Tm diag(beta e^G) and Tm diag(beta) as split K-major images [t][s]
+        for (int e = tid; e < C * 8; e += 256) {
+            const int t = e >> 3, j8 = e & 7;
+            uint4 wh, wl, bh, bl;
+            uint32_t *whp = &wh.x, *wlp = &wl.x, *bhp = &bh.x, *blp = &bl.x;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int s2 = 8 * j8 + 2 * k;
+                const float v0 = sm.tm[t][s2], v1 = sm.tm[t][s2 + 1];
+                const float cb0 = bcur[s2], cb1 = bcur[s2 + 1];
+                split2_bf16(v0 * cb0 * sm.eG[s2], v1 * cb1 * sm.eG[s2 + 1], whp[k], wlp[k]);
+                split2_bf16(v0 * cb0, v1 * cb1, bhp[k], blp[k]);
+            }
+            const uint32_t off = sw128_off_b16((uint32_t)t, (uint32_t)(8 * j8));
+            *reinterpret_cast<uint4*>(tmw + off) = wh;
+            *reinterpret_cast<uint4*>(tmw + 8192 + off) = wl;
+            *reinterpret_cast<uint4*>(tmb + off) = bh;
+            *reinterpret_cast<uint4*>(tmb + 8192 + off) = bl;
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        // ---- W^T = K^T TmW^T and U0^T = V^T TmB^T  (M 128 over k / v, N 64, K 64; A MN-major)
+        if (tid == 0) {
+            if (wait_or_flag(&sm.bar_v, ph, err, ok)) {
+                fence_after_sync();
+                constexpr uint32_t ID = idesc_bf16(128, 64, false, true);
+                // A: rows s (128 B of d each) of the 16 KB d-boxes; K at row 0, V at row 64
+                const uint64_t kh_ = sw128_desc(kq_hi, 16384, 1024), kl_ = sw128_desc(kq_lo, 16384, 1024);
+                const uint64_t wh_ = sw128_desc(smem_u32(tmw), 16, 1024), wl_ = wh_ + (8192 >> 4);
+                const uint64_t bh_ = sw128_desc(smem_u32(tmb), 16, 1024), bl_ = bh_ + (8192 >> 4);
+#pragma unroll
+                for (int pass = 0; pass < 3; ++pass) {
+                    const uint64_t a = pass == 2 ? kl_ : kh_, bb = pass == 1 ? wl_ : wh_;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        umma_ss(tmem + I_W, a + (uint64_t)((ks * 2048) >> 4), bb + (uint64_t)((ks * 32) >> 4), ID,
+                                (pass | ks) != 0);
+                }
+#pragma unroll
+                for (int pass = 0; pass < 3; ++pass) {
+                    const uint64_t a = (pass == 2 ? kl_ : kh_) + (8192 >> 4), bb = pass == 1 ? bl_ : bh_;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        umma_ss(tmem + I_U0, a + (uint64_t)((ks * 2048) >> 4), bb + (uint64_t)((ks * 32) >> 4), ID,
+                                (pass | ks) != 0);
+                }
+                umma_commit(&sm.bar_m2);
+            }
+        }
+        wait_or_flag(&sm.bar_m2, ph, err, ok);
+        if (!__syncthreads_and(ok)) break;
+        fence_after_sync();
+        // ---- epilogue 2: W images and the U0^T image into this buffer, then one bulk store
+        unsigned char* img = reinterpret_cast<unsigned char*>(&sm.kq[buf][0][0][0][0]);
+        {
+            float x[32];
+            // W^T: lane = k, columns t in [32h, 32h + 32) -> W[t][k]; lane pairs (k, k+1) make one word
+            tmem_ld32(lane_addr + I_W + 32 * h, x);
+            const uint32_t kb = (uint32_t)row >> 6, kc = (uint32_t)row & 62u;
+            const bool odd = (lane & 1) != 0;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-                __nv_bfloat16 hi, lo;
-                split_bf16(x[j], hi, lo);
+                uint32_t hi, lo;
+                split2_bf16(x[j], 0.0f, hi, lo);                   // low halves = this lane's value
+                const uint32_t ph_ = __shfl_xor_sync(0xffffffffu, odd ? hi : lo, 1);
+                // even lane: (own hi, partner hi) ; odd lane: (partner lo, own lo)
+                const uint32_t word = odd ? ((lo & 0xFFFFu) << 16) | (ph_ & 0xFFFFu)
+                                          : (hi & 0xFFFFu) | ((ph_ & 0xFFFFu) << 16);
                 const uint32_t off = kb * 8192u + sw128_off_b16((uint32_t)(32 * h + j), kc);
-                *reinterpret_cast<__nv_bfloat16*>(img + off) = hi;
-                *reinterpret_cast<__nv_bfloat16*>(img + 16384 + off) = lo;
+                *reinterpret_cast<uint32_t*>(img + (odd ? 16384u : 0u) + off) = word;
             }
-        }
-        // U0^T: lane = v, columns t in [32h, 32h + 32) -> t-box h of the f32 image
-        tmem_ld32(lane_addr + I_U0 + 32 * h, x);
+            // U0^T: lane = v, columns t in [32h, 32h + 32) -> t-box h of the f32 image
+            tmem_ld32(lane_addr + I_U0 + 32 * h, x);
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4)
-            *reinterpret_cast<float4*>(img + REC_U0 + (uint32_t)h * 16384u + sw128_off_b32((uint32_t)row, 4u * j4)) =
-                make_float4(x[4 * j4], x[4 * j4 + 1], x[4 * j4 + 2], x[4 * j4 + 3]);
+            for (int j4 = 0; j4 < 8; ++j4)
+                *reinterpret_cast<float4*>(img + REC_U0 + (uint32_t)h * 16384u + sw128_off_b32((uint32_t)row, 4u * j4)) =
+                    make_float4(x[4 * j4], x[4 * j4 + 1], x[4 * j4 + 2], x[4 * j4 + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            bulk_s2g(R + REC_W, img, 65536);
+            bulk_commit();
+        }
+        (void)kh;
     }
-    fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0 && ok) {
-        unsigned char* R = rec + ((size_t)c * vc + vl) * REC_BYTES;
-        bulk_s2g(R + REC_W, img, 65536);
-        bulk_s2g(R + REC_P, &sm.p[0][0][0], 16384);
-        bulk_s2g(R + REC_G, sm.G, 256);
-        bulk_commit();
-        bulk_wait_all();
-    }
+    if (tid == 0) bulk_wait_all();
     fence_before_sync();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 256);
@@ -420,36 +491,39 @@ __global__ void __launch_bounds__(256, 1) gdn_pf_intra_kernel(const __grid_const
 // ---------------------------------------------------------------------------
 namespace gp {
 struct alignas(1024) ChainSmem {
-    unsigned char w[32768];      // record: W images [hi|lo][k-box][64 t][64 k]
-    unsigned char u0t[32768];    // record: U0^T image [t-box][128 v][32 t]
+    // B operand of the S product, per chunk parity: [hi|lo][k-box][128 rows][64 k],
+    // rows 0-63 = Q of the chunk (TMA), rows 64-127 = W (record)
+    unsigned char wq[2][65536];
+    // B operand of the state update, per chunk parity: K [hi|lo][d-box][64 t][64 d]
+    // (TMA), scaled in place by e^{G_last - G_t}
+    unsigned char kd[2][32768];
     unsigned char p[16384];      // record: P images [hi|lo][64 t][64 s]
-    unsigned char qe[32768];     // Q [hi|lo][d-box][64 t][64 d] as loaded, scaled in place to Q e^G
-    unsigned char kd[32768];     // K e^{G_last - G}, same layout (B operand, MN-major)
-    unsigned char kraw[32768];   // K as loaded
-    float zt[C][D];              // z rows of the chunk for this head [t][v] (TMA, zero past T)
-    float gring[4][C];           // G of chunks c % 4
+    float gring[8][C];           // G of chunks c % 8
+    float eg[C];                 // e^{G_t} of the chunk in the y epilogue
     float red[4][C];             // per-warp partial sums of y^2 per token
-    float inv[C];                // 1 / rms per token
-    uint64_t full_w, full_u0, full_p, full_q, full_k, full_z, full_g[4];
-    uint64_t mma1_done, dy1_done, mma3_done;
-    uint64_t mma2_done[2], y_free[2];   // per D_Y buffer (chunk parity): one completion every 2 chunks
-    uint64_t s_ready, u_ready, qe_ready, kd_ready, z_free;
+    uint64_t full_wq[2], full_k[2], full_p, full_g[8];
+    uint64_t mma1_done[2], mma3_done[2], mma2_done;
+    uint64_t s_ready, u_ready, kd_ready[2], yp_free, yu_free;
     uint32_t tmem_base;
 };
 // TMEM columns of the chain kernel (512 allocated)
 constexpr uint32_t S_ACC = 0;    // f32 state [v lane][k], holds e^{G_last} S between the S epilogue and MMA3
 constexpr uint32_t S_HI = 128;   // bf16 pairs of S (A operand), 64 columns
 constexpr uint32_t S_LO = 192;
-constexpr uint32_t D_U = 256;    // S W^T, f32 [v][t]
-constexpr uint32_t U_HI = 320;   // bf16 pairs of U^T (A operand), 32 columns
-constexpr uint32_t U_LO = 352;
-constexpr uint32_t D_Y = 384;    // Y^T f32 [v][t], two buffers (chunk parity) at 384 and 448
+constexpr uint32_t D_YP = 256;   // S Q^T  [v][t]   } one N = 128 product
+constexpr uint32_t D_U = 320;    // S W^T  [v][t]   }
+constexpr uint32_t U_HI = 384;   // bf16 pairs of U^T (A operand), 32 columns
+constexpr uint32_t U_LO = 416;
+constexpr uint32_t D_YU = 448;   // U^T P^T [v][t]
 // warp roles
-constexpr int EY_W0 = 0;         // warps 0-3: y epilogue (gated RMSNorm, store)
-constexpr int E1_W0 = 4;         // warps 4-11: U and S epilogues (the serial path)
-constexpr int ES_W0 = 12;        // warps 12-15: Q e^G and K e^{G_last - G} scaling
-constexpr int CTL_W = 16;        // warp 16: lane 0 loads, lane 1 issues MMAs
-constexpr int CHAIN_THREADS = 17 * 32;
+constexpr int EY_W0 = 0;         // warps 0-7: y epilogue (gated RMSNorm, store), tokens split in halves
+constexpr int E1_W0 = 8;         // warps 8-15: U and S epilogues (the serial path)
+constexpr int ES_W0 = 16;        // warps 16-17: K e^{G_last - G} scaling
+constexpr int ES_THREADS = 64;
+constexpr int LD_W = 18;         // warp 18, lane 0: loads
+constexpr int MMA_W = 19;        // warp 19, lane 0: issues the tensor-core products
+constexpr int CHAIN_THREADS = 20 * 32;   // 5 warps per SM sub-partition: up to 96 registers a thread
+constexpr int BAR_EY = 1;        // named barrier of the y-epilogue warps (0 is __syncthreads)
 }  // namespace gp
 
 __device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
@@ -460,6 +534,7 @@ __device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
         : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(nthreads) : "memory");
     return r != 0;
 }
+
 
 // One halving step of a warp reduce-scatter: N values per lane -> N/2, lanes
 // with BIT set keep (and sum) the upper half.
@@ -474,35 +549,21 @@ __device__ __forceinline__ void bfly_reduce(float* a, int lane) {
     }
 }
 
-// scale each 128-byte row t of a [hi|lo][d-box][64][64] bf16 image by f(t), re-splitting hi/lo
-template <typename F>
-__device__ __forceinline__ void scale_rows(const unsigned char* src, unsigned char* dst, int tid, int nthr, F f) {
-    for (int i = tid; i < 1024; i += nthr) {          // 16-byte chunks of the hi image
-        const uint32_t off = (uint32_t)i * 16u;
-        const int t = (int)((off & 8191u) >> 7);
-        const float sc = f(t);
-        const uint4 h = *reinterpret_cast<const uint4*>(src + off);
-        const uint4 l = *reinterpret_cast<const uint4*>(src + 16384 + off);
-        const uint32_t* hp = &h.x;
-        const uint32_t* lp = &l.x;
-        uint4 nh, nl;
-        uint32_t* nhp = &nh.x;
-        uint32_t* nlp = &nl.x;
+// silu with the fast exponential and division (relative error ~1e-6)
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// U0^T of one record, row v, t in [32h, 32h + 32): eight 16-byte chunks whose
+// positions in the image are XOR-swizzled by v % 8
+__device__ __forceinline__ void load_u0(const unsigned char* rec_u0, int v, int h, float4 (&u)[8]) {
+    const unsigned char* row = rec_u0 + (size_t)h * 16384 + (size_t)v * 128;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float a = (tc::bf16_lo_f(hp[e]) + tc::bf16_lo_f(lp[e])) * sc;
-            const float b = (tc::bf16_hi_f(hp[e]) + tc::bf16_hi_f(lp[e])) * sc;
-            tc::split2_bf16(a, b, nhp[e], nlp[e]);
-        }
-        *reinterpret_cast<uint4*>(dst + off) = nh;
-        *reinterpret_cast<uint4*>(dst + 16384 + off) = nl;
-    }
+    for (int j = 0; j < 8; ++j) u[j] = __ldg(reinterpret_cast<const float4*>(row + ((j ^ (v & 7)) << 4)));
 }
 
 __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
-    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-    const __grid_constant__ CUtensorMap tm_z, int64_t T, int NC, int vh0, int vc, const unsigned char* __restrict__ rec,
-    float* __restrict__ state, const float* __restrict__ norm_w, float* __restrict__ y_out, int* err) {
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, int64_t T, int NC, int vh0,
+    int vc, const unsigned char* __restrict__ rec, float* __restrict__ state, const float* __restrict__ z,
+    const float* __restrict__ norm_w, float* __restrict__ y_out, int* err) {
     using namespace gp;
     using namespace tc;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -512,19 +573,22 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
     const int kh = (vh0 + vl) % SSM_HK;
     auto R = [&](int c) { return rec + ((size_t)c * vc + vl) * REC_BYTES; };
 
-    if (warp == CTL_W) tmem_alloc(&sm.tmem_base, 512);
+    if (warp == MMA_W) tmem_alloc(&sm.tmem_base, 512);
     if (tid == 0) {
-        uint64_t* one[11] = {&sm.full_w, &sm.full_u0, &sm.full_p, &sm.full_q, &sm.full_k, &sm.full_z,
-                             &sm.mma1_done, &sm.dy1_done, &sm.mma3_done, &sm.mma2_done[0], &sm.mma2_done[1]};
-        for (uint64_t* b : one) mbar_init(b, 1);
-        for (int i = 0; i < 4; ++i) mbar_init(&sm.full_g[i], 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sm.full_wq[i], 1);
+            mbar_init(&sm.full_k[i], 1);
+            mbar_init(&sm.mma1_done[i], 1);
+            mbar_init(&sm.mma3_done[i], 1);
+            mbar_init(&sm.kd_ready[i], ES_THREADS);
+        }
+        for (int i = 0; i < 8; ++i) mbar_init(&sm.full_g[i], 1);
+        mbar_init(&sm.full_p, 1);
+        mbar_init(&sm.mma2_done, 1);
         mbar_init(&sm.s_ready, 256);
         mbar_init(&sm.u_ready, 256);
-        mbar_init(&sm.qe_ready, 128);
-        mbar_init(&sm.kd_ready, 128);
-        mbar_init(&sm.y_free[0], 128);
-        mbar_init(&sm.y_free[1], 128);
-        mbar_init(&sm.z_free, 128);
+        mbar_init(&sm.yp_free, 256);
+        mbar_init(&sm.yu_free, 256);
         fence_mbar_init();
     }
     fence_before_sync();
@@ -533,109 +597,101 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
     const uint32_t tmem = sm.tmem_base;
     bool ok = true;
 
-    if (warp == CTL_W) {
+    if (warp == LD_W) {
         if (lane == 0) {
             // ---------------- loader ----------------
-            for (int c = 0; c < NC && c < 3; ++c) {
+            // Buffers of parity b are reused by chunk c + 2 once chunk c's readers are
+            // done: WQ after MMA1(c), KD after MMA3(c) (per-parity barriers, one
+            // completion every two chunks); P after MMA2(c-1).  G slots are 8 chunks
+            // apart; slot (c+5)%8 held chunk c-3, whose last reader (the y epilogue)
+            // finished before MMA1(c-2).
+            for (int c = 0; c < NC && c < 5; ++c) {
                 mbar_arrive_expect_tx(&sm.full_g[c], 256);
                 bulk_g2s(sm.gring[c], R(c) + REC_G, 256, &sm.full_g[c]);
             }
             for (int c = 0; c < NC && ok; ++c) {
-                const uint32_t pp = (uint32_t)((c - 1) & 1);
+                const int b = c & 1;
+                const uint32_t pp2 = (uint32_t)(((c - 2) >> 1) & 1);
                 const int t0 = c * C;
-                if (c > 0 && !wait_or_flag(&sm.kd_ready, pp, err, ok)) break;
-                mbar_arrive_expect_tx(&sm.full_k, 32768);
+                // K(c) -> KD[b]
+                if (c > 1 && !wait_or_flag(&sm.mma3_done[b], pp2, err, ok)) break;
+                mbar_arrive_expect_tx(&sm.full_k[b], 32768);
                 for (int hl = 0; hl < 2; ++hl)
                     for (int db = 0; db < 2; ++db)
-                        tma_load_4d(sm.kraw + hl * 16384 + db * 8192, &tm_k, 64 * db, t0, hl, kh, &sm.full_k);
-                if (c > 0 && !wait_or_flag(&sm.mma1_done, pp, err, ok)) break;
-                mbar_arrive_expect_tx(&sm.full_w, 32768);
-                bulk_g2s(sm.w, R(c) + REC_W, 32768, &sm.full_w);
-                if (c > 0 && !wait_or_flag(&sm.u_ready, pp, err, ok)) break;
-                mbar_arrive_expect_tx(&sm.full_u0, 32768);
-                bulk_g2s(sm.u0t, R(c) + REC_U0, 32768, &sm.full_u0);
-                if (c > 0 && !wait_or_flag(&sm.dy1_done, pp, err, ok)) break;
-                mbar_arrive_expect_tx(&sm.full_q, 32768);
+                        tma_load_4d(sm.kd[b] + hl * 16384 + db * 8192, &tm_k, 64 * db, t0, hl, kh, &sm.full_k[b]);
+                // Q(c) and W(c) -> WQ[b]
+                if (c > 1 && !wait_or_flag(&sm.mma1_done[b], pp2, err, ok)) break;
+                if (c + 5 < NC) {
+                    const int s = (c + 5) & 7;
+                    mbar_arrive_expect_tx(&sm.full_g[s], 256);
+                    bulk_g2s(sm.gring[s], R(c + 5) + REC_G, 256, &sm.full_g[s]);
+                }
+                mbar_arrive_expect_tx(&sm.full_wq[b], 65536);
                 for (int hl = 0; hl < 2; ++hl)
-                    for (int db = 0; db < 2; ++db)
-                        tma_load_4d(sm.qe + hl * 16384 + db * 8192, &tm_q, 64 * db, t0, hl, kh, &sm.full_q);
-                if (c > 0 && !wait_or_flag(&sm.mma2_done[(c - 1) & 1], (uint32_t)(((c - 1) >> 1) & 1), err, ok)) break;
+                    for (int kb = 0; kb < 2; ++kb) {
+                        unsigned char* box = sm.wq[b] + hl * 32768 + kb * 16384;
+                        tma_load_4d(box, &tm_q, 64 * kb, t0, hl, kh, &sm.full_wq[b]);
+                        bulk_g2s(box + 8192, R(c) + REC_W + hl * 16384 + kb * 8192, 8192, &sm.full_wq[b]);
+                    }
+                // P(c)
+                if (c > 0 && !wait_or_flag(&sm.mma2_done, (uint32_t)((c - 1) & 1), err, ok)) break;
                 mbar_arrive_expect_tx(&sm.full_p, 16384);
                 bulk_g2s(sm.p, R(c) + REC_P, 16384, &sm.full_p);
-                if (c > 0 && !wait_or_flag(&sm.z_free, pp, err, ok)) break;
-                mbar_arrive_expect_tx(&sm.full_z, C * D * 4);
-                tma_load_2d(&sm.zt[0][0], &tm_z, (vh0 + vl) * D, t0, &sm.full_z);
-                // G of chunk c+3 into slot (c+3)%4 (chunk c-1's G: every reader finished before MMA2(c-1))
-                if (c + 3 < NC) {
-                    const int s = (c + 3) & 3;
-                    mbar_arrive_expect_tx(&sm.full_g[s], 256);
-                    bulk_g2s(sm.gring[s], R(c + 3) + REC_G, 256, &sm.full_g[s]);
-                }
             }
-        } else if (lane == 1) {
+        }
+    } else if (warp == MMA_W) {
+        if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            constexpr uint32_t ID64 = idesc_bf16(128, 64, false);
+            constexpr uint32_t ID128 = idesc_bf16(128, 128, false);
             constexpr uint32_t ID128MN = idesc_bf16(128, 128, true);
-            const uint32_t w_s = smem_u32(sm.w), q_s = smem_u32(sm.qe), k_s = smem_u32(sm.kd), p_s = smem_u32(sm.p);
+            constexpr uint32_t ID64 = idesc_bf16(128, 64, false);
+            // descriptors of the buffers' first bytes; an offset of o bytes adds o >> 4
+            // (shared-memory addresses stay below 256 KB, inside the 14-bit field)
+            const uint64_t dwq0 = sw128_desc(smem_u32(sm.wq[0]), 16, 1024);
+            const uint64_t dkd0 = sw128_desc(smem_u32(sm.kd[0]), 8192, 1024);
+            const uint64_t dp0 = sw128_desc(smem_u32(sm.p), 16, 1024);
             for (int c = 0; c < NC && ok; ++c) {
-                const uint32_t ph = (uint32_t)(c & 1);
-                // U-part: D_U = S W^T  (A = S hi/lo from TMEM, B = W images, N 64, K 128)
-                if (!wait_or_flag(&sm.s_ready, ph, err, ok) || !wait_or_flag(&sm.full_w, ph, err, ok)) break;
+                const int b = c & 1;
+                const uint32_t ph = (uint32_t)(c & 1), pb = (uint32_t)((c >> 1) & 1);
+                // [D_YP | D_U] = S [Q; W]^T  (A = S hi/lo in TMEM, N 128, K 128)
+                if (!wait_or_flag(&sm.s_ready, ph, err, ok) || !wait_or_flag(&sm.full_wq[b], pb, err, ok)) break;
+                if (c > 0 && !wait_or_flag(&sm.yp_free, (uint32_t)((c - 1) & 1), err, ok)) break;
                 fence_after_sync();
-                {
-                    uint32_t acc = 0;
-                    for (int pass = 0; pass < 3; ++pass) {
-                        const uint32_t a = pass == 2 ? S_LO : S_HI, b = w_s + (pass == 1 ? 16384u : 0u);
 #pragma unroll
-                        for (int ks = 0; ks < 8; ++ks) {
-                            umma_ts(tmem + D_U, tmem + a + 8u * ks,
-                                    sw128_desc(b + (uint32_t)(ks >> 2) * 8192u + (uint32_t)(ks & 3) * 32u, 16, 1024),
-                                    ID64, acc);
-                            acc = 1;
-                        }
-                    }
-                }
-                umma_commit(&sm.mma1_done);
-                // Y-part 1: D_Y = S Qe^T
-                if (!wait_or_flag(&sm.qe_ready, ph, err, ok)) break;
-                if (c > 1 && !wait_or_flag(&sm.y_free[c & 1], (uint32_t)(((c - 2) >> 1) & 1), err, ok)) break;
-                const uint32_t dy = D_Y + 64u * (uint32_t)(c & 1);
-                fence_after_sync();
-                {
-                    uint32_t acc = 0;
-                    for (int pass = 0; pass < 3; ++pass) {
-                        const uint32_t a = pass == 2 ? S_LO : S_HI, b = q_s + (pass == 1 ? 16384u : 0u);
-#pragma unroll
-                        for (int ks = 0; ks < 8; ++ks) {
-                            umma_ts(tmem + dy, tmem + a + 8u * ks,
-                                    sw128_desc(b + (uint32_t)(ks >> 2) * 8192u + (uint32_t)(ks & 3) * 32u, 16, 1024),
-                                    ID64, acc);
-                            acc = 1;
-                        }
-                    }
-                }
-                umma_commit(&sm.dy1_done);
-                // state: S_ACC (= e^{G_last} S) += U^T Kd  (B = Kd MN-major, N 128, K 64)
-                if (!wait_or_flag(&sm.u_ready, ph, err, ok) || !wait_or_flag(&sm.kd_ready, ph, err, ok)) break;
-                fence_after_sync();
                 for (int pass = 0; pass < 3; ++pass) {
-                    const uint32_t a = pass == 2 ? U_LO : U_HI, b = k_s + (pass == 1 ? 16384u : 0u);
+                    const uint32_t a = pass == 2 ? S_LO : S_HI;
+                    const uint64_t bd = dwq0 + (uint64_t)((b * 65536 + (pass == 1 ? 32768 : 0)) >> 4);
+#pragma unroll
+                    for (int ks = 0; ks < 8; ++ks)
+                        umma_ts(tmem + D_YP, tmem + a + 8u * ks, bd + (uint64_t)(((ks >> 2) * 16384 + (ks & 3) * 32) >> 4),
+                                ID128, (pass | ks) != 0);
+                }
+                umma_commit(&sm.mma1_done[b]);
+                // S_ACC (= e^{G_last} S) += U^T Kd  (A = U hi/lo, B = Kd MN-major, N 128, K 64)
+                if (!wait_or_flag(&sm.u_ready, ph, err, ok) || !wait_or_flag(&sm.kd_ready[b], pb, err, ok)) break;
+                fence_after_sync();
+#pragma unroll
+                for (int pass = 0; pass < 3; ++pass) {
+                    const uint32_t a = pass == 2 ? U_LO : U_HI;
+                    const uint64_t bd = dkd0 + (uint64_t)((b * 32768 + (pass == 1 ? 16384 : 0)) >> 4);
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_ts(tmem + S_ACC, tmem + a + 8u * ks, sw128_desc(b + (uint32_t)ks * 2048u, 8192, 1024),
-                                ID128MN, 1);
+                        umma_ts(tmem + S_ACC, tmem + a + 8u * ks, bd + (uint64_t)((ks * 2048) >> 4), ID128MN, 1);
                 }
-                umma_commit(&sm.mma3_done);
-                // Y-part 2: D_Y += U^T P^T  (B = P images, N 64, K 64)
+                umma_commit(&sm.mma3_done[b]);
+                // D_YU = U^T P^T  (B = P images, N 64, K 64)
                 if (!wait_or_flag(&sm.full_p, ph, err, ok)) break;
+                if (c > 0 && !wait_or_flag(&sm.yu_free, (uint32_t)((c - 1) & 1), err, ok)) break;
                 fence_after_sync();
+#pragma unroll
                 for (int pass = 0; pass < 3; ++pass) {
-                    const uint32_t a = pass == 2 ? U_LO : U_HI, b = p_s + (pass == 1 ? 8192u : 0u);
+                    const uint32_t a = pass == 2 ? U_LO : U_HI;
+                    const uint64_t bd = dp0 + (uint64_t)((pass == 1 ? 8192 : 0) >> 4);
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_ts(tmem + dy, tmem + a + 8u * ks, sw128_desc(b + (uint32_t)ks * 32u, 16, 1024), ID64, 1);
+                        umma_ts(tmem + D_YU, tmem + a + 8u * ks, bd + (uint64_t)((ks * 32) >> 4), ID64, (pass | ks) != 0);
                 }
-                umma_commit(&sm.mma2_done[c & 1]);
+                umma_commit(&sm.mma2_done);
             }
         }
     } else if (warp >= E1_W0 && warp < ES_W0) {
@@ -647,11 +703,12 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
         // initial state: S_HI/S_LO <- split(S0), S_ACC <- e^{G_last(0)} S0
         if (wait_or_flag(&sm.full_g[0], 0, err, ok)) {
             const float e0 = expf(sm.gring[0][C - 1]);
-            for (int piece = 0; piece < 2; ++piece) {
-                const int k0 = 64 * h + 32 * piece;
-                uint32_t hi[16], lo[16], sc[32];
+#pragma unroll 1
+            for (int piece = 0; piece < 4; ++piece) {
+                const int k0 = 64 * h + 16 * piece;
+                uint32_t hi[8], lo[8], sc[16];
 #pragma unroll
-                for (int j4 = 0; j4 < 8; ++j4) {
+                for (int j4 = 0; j4 < 4; ++j4) {
                     const float4 s4 = *reinterpret_cast<const float4*>(Sg + k0 + 4 * j4);
                     split2_bf16(s4.x, s4.y, hi[2 * j4], lo[2 * j4]);
                     split2_bf16(s4.z, s4.w, hi[2 * j4 + 1], lo[2 * j4 + 1]);
@@ -660,29 +717,33 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
                     sc[4 * j4 + 2] = __float_as_uint(s4.z * e0);
                     sc[4 * j4 + 3] = __float_as_uint(s4.w * e0);
                 }
-                tmem_st16_async(la + S_HI + (uint32_t)(k0 >> 1), hi);
-                tmem_st16_async(la + S_LO + (uint32_t)(k0 >> 1), lo);
-                tmem_st32_async(la + S_ACC + (uint32_t)k0, sc);
+                tmem_st8_async(la + S_HI + (uint32_t)(k0 >> 1), hi);
+                tmem_st8_async(la + S_LO + (uint32_t)(k0 >> 1), lo);
+                tmem_st16_async(la + S_ACC + (uint32_t)k0, sc);
+                tmem_wait_st();
             }
-            tmem_wait_st();
         }
         fence_before_sync();
         mbar_arrive(&sm.s_ready);
+        float4 u0[8];
+        load_u0(R(0) + REC_U0, v, h, u0);
         for (int c = 0; c < NC && ok; ++c) {
-            const uint32_t ph = (uint32_t)(c & 1);
+            const int b = c & 1;
+            const uint32_t pb = (uint32_t)((c >> 1) & 1);
             // U^T = U0^T - S W^T  -> bf16 pairs (columns t in [32h, 32h + 32))
-            if (!wait_or_flag(&sm.mma1_done, ph, err, ok) || !wait_or_flag(&sm.full_u0, ph, err, ok)) break;
+            if (!wait_or_flag(&sm.mma1_done[b], pb, err, ok)) break;
             fence_after_sync();
             {
-                float x[32];
-                tmem_ld32(la + D_U + 32u * h, x);
+                uint32_t r[32];
+                tmem_ld32_async(la + D_U + 32u * h, r);
+                tmem_wait_ld();
                 uint32_t hi[16], lo[16];
-                const unsigned char* u0 = sm.u0t + (uint32_t)h * 16384u;
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
-                    const float4 a = *reinterpret_cast<const float4*>(u0 + sw128_off_b32((uint32_t)v, 4u * j4));
-                    split2_bf16(a.x - x[4 * j4], a.y - x[4 * j4 + 1], hi[2 * j4], lo[2 * j4]);
-                    split2_bf16(a.z - x[4 * j4 + 2], a.w - x[4 * j4 + 3], hi[2 * j4 + 1], lo[2 * j4 + 1]);
+                    split2_bf16(u0[j4].x - __uint_as_float(r[4 * j4]), u0[j4].y - __uint_as_float(r[4 * j4 + 1]),
+                                hi[2 * j4], lo[2 * j4]);
+                    split2_bf16(u0[j4].z - __uint_as_float(r[4 * j4 + 2]), u0[j4].w - __uint_as_float(r[4 * j4 + 3]),
+                                hi[2 * j4 + 1], lo[2 * j4 + 1]);
                 }
                 tmem_st16_async(la + U_HI + 16u * h, hi);
                 tmem_st16_async(la + U_LO + 16u * h, lo);
@@ -690,127 +751,157 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
             }
             fence_before_sync();
             mbar_arrive(&sm.u_ready);
+            // the next chunk's U0^T row: into L2 now, into registers after the S epilogue
+            if (c + 1 < NC)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(R(c + 1) + REC_U0 + (size_t)h * 16384 + (size_t)v * 128));
             // S epilogue: S_{c+1} -> S_HI/S_LO and S_ACC <- e^{G_last(c+1)} S_{c+1}; or the final state
-            if (!wait_or_flag(&sm.mma3_done, ph, err, ok)) break;
+            if (!wait_or_flag(&sm.mma3_done[b], pb, err, ok)) break;
             fence_after_sync();
             const bool last = c + 1 == NC;
             float e1 = 1.0f;
             if (!last) {
-                const int s = (c + 1) & 3;
-                if (!wait_or_flag(&sm.full_g[s], (uint32_t)(((c + 1) >> 2) & 1), err, ok)) break;
+                const int s = (c + 1) & 7;
+                if (!wait_or_flag(&sm.full_g[s], (uint32_t)(((c + 1) >> 3) & 1), err, ok)) break;
                 e1 = expf(sm.gring[s][C - 1]);
             }
-            for (int piece = 0; piece < 2; ++piece) {
-                const int k0 = 64 * h + 32 * piece;
-                uint32_t r[32];
-                tmem_ld32_async(la + S_ACC + (uint32_t)k0, r);
+#pragma unroll 1
+            for (int piece = 0; piece < 4; ++piece) {
+                const int k0 = 64 * h + 16 * piece;
+                uint32_t r[16];
+                tmem_ld16_async(la + S_ACC + (uint32_t)k0, r);
                 tmem_wait_ld();
                 if (last) {
 #pragma unroll
-                    for (int j4 = 0; j4 < 8; ++j4)
+                    for (int j4 = 0; j4 < 4; ++j4)
                         *reinterpret_cast<float4*>(Sg + k0 + 4 * j4) =
                             make_float4(__uint_as_float(r[4 * j4]), __uint_as_float(r[4 * j4 + 1]),
                                         __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3]));
                 } else {
-                    uint32_t hi[16], lo[16];
+                    uint32_t hi[8], lo[8];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
+                    for (int j = 0; j < 8; ++j)
                         split2_bf16(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]), hi[j], lo[j]);
-                    tmem_st16_async(la + S_HI + (uint32_t)(k0 >> 1), hi);
-                    tmem_st16_async(la + S_LO + (uint32_t)(k0 >> 1), lo);
+                    tmem_st8_async(la + S_HI + (uint32_t)(k0 >> 1), hi);
+                    tmem_st8_async(la + S_LO + (uint32_t)(k0 >> 1), lo);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * e1);
-                    tmem_st32_async(la + S_ACC + (uint32_t)k0, r);
+                    for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * e1);
+                    tmem_st16_async(la + S_ACC + (uint32_t)k0, r);
                 }
             }
             if (!last) {
                 tmem_wait_st();
                 fence_before_sync();
                 mbar_arrive(&sm.s_ready);
+                load_u0(R(c + 1) + REC_U0, v, h, u0);
             }
         }
-    } else if (warp >= ES_W0) {
-        // ---------------- Q e^G and K e^{G_last - G} ----------------
+    } else if (warp >= ES_W0 && warp < LD_W) {
+        // ---------------- K e^{G_last - G}, in place ----------------
         const int et = tid - ES_W0 * 32;
         for (int c = 0; c < NC && ok; ++c) {
-            const uint32_t ph = (uint32_t)(c & 1);
-            const int s = c & 3;
-            if (!wait_or_flag(&sm.full_g[s], (uint32_t)((c >> 2) & 1), err, ok)) break;
+            const int b = c & 1, s = c & 7;
+            if (!wait_or_flag(&sm.full_g[s], (uint32_t)((c >> 3) & 1), err, ok)) break;
+            if (!wait_or_flag(&sm.full_k[b], (uint32_t)((c >> 1) & 1), err, ok)) break;
             const float* G = sm.gring[s];
-            if (!wait_or_flag(&sm.full_q, ph, err, ok)) break;
-            scale_rows(sm.qe, sm.qe, et, 128, [&](int t) { return expf(G[t]); });
-            fence_proxy_async_smem();
-            mbar_arrive(&sm.qe_ready);
-            if (!wait_or_flag(&sm.full_k, ph, err, ok)) break;
-            if (c > 0 && !wait_or_flag(&sm.mma3_done, (uint32_t)((c - 1) & 1), err, ok)) break;
             const float Gl = G[C - 1];
-            scale_rows(sm.kraw, sm.kd, et, 128, [&](int t) { return expf(Gl - G[t]); });
+            unsigned char* img = sm.kd[b];
+            for (int i = et; i < 1024; i += ES_THREADS) {   // 16-byte chunks of the hi image
+                const uint32_t off = (uint32_t)i * 16u;
+                const float sc = __expf(Gl - G[(off & 8191u) >> 7]);
+                uint4 hq = *reinterpret_cast<const uint4*>(img + off);
+                uint4 lq = *reinterpret_cast<const uint4*>(img + 16384 + off);
+                uint32_t* hp = &hq.x;
+                uint32_t* lp = &lq.x;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float a = (bf16_lo_f(hp[e]) + bf16_lo_f(lp[e])) * sc;
+                    const float bb = (bf16_hi_f(hp[e]) + bf16_hi_f(lp[e])) * sc;
+                    split2_bf16(a, bb, hp[e], lp[e]);
+                }
+                *reinterpret_cast<uint4*>(img + off) = hq;
+                *reinterpret_cast<uint4*>(img + 16384 + off) = lq;
+            }
             fence_proxy_async_smem();
-            mbar_arrive(&sm.kd_ready);
+            mbar_arrive(&sm.kd_ready[b]);
         }
     } else {
-        // ---------------- y epilogue: gated RMSNorm of Y^T, thread = v ----------------
-        const int ew = warp - EY_W0;
-        const int v = 32 * ew + lane;
-        const uint32_t la = tmem + ((uint32_t)(32 * ew) << 16);
+        // ---------------- y epilogue: y = e^G o (S Q^T) + U^T P^T, gated RMSNorm, store ----------------
+        const int q4 = (warp - EY_W0) & 3, th = (warp - EY_W0) >> 2;   // lanes 32 q4.., tokens [32 th, 32 th + 32)
+        const int v = 32 * q4 + lane;
+        const uint32_t la = tmem + ((uint32_t)(32 * q4) << 16);
         const float wv = norm_w[v];
+        const float* zb = z + (size_t)(vh0 + vl) * D + v;
         float* yb = y_out + (size_t)vl * D + v;
         for (int c = 0; c < NC; ++c) {
-            const bool got = ok && wait_or_flag(&sm.mma2_done[c & 1], (uint32_t)((c >> 1) & 1), err, ok);
-            if (!named_bar_and(1, 128, got)) {
+            const int b = c & 1, s = c & 7;
+            // S Q^T of the chunk, as soon as the S product is done
+            bool got = ok && wait_or_flag(&sm.full_g[s], (uint32_t)((c >> 3) & 1), err, ok) &&
+                       wait_or_flag(&sm.mma1_done[b], (uint32_t)((c >> 1) & 1), err, ok);
+            if (!named_bar_and(BAR_EY, 256, got)) {
                 ok = false;
                 break;
             }
             fence_after_sync();
-            float y[C];
+            float y[32];
             {
                 uint32_t r[32];
-                const uint32_t dy = D_Y + 64u * (uint32_t)(c & 1);
-                tmem_ld32_async(la + dy, r);
+                tmem_ld32_async(la + D_YP + 32u * th, r);
                 tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) y[j] = __uint_as_float(r[j]);
-                tmem_ld32_async(la + dy + 32u, r);
+            }
+            if (tid < C) sm.eg[tid] = __expf(sm.gring[s][tid]);
+            fence_before_sync();
+            mbar_arrive(&sm.yp_free);
+            got = ok && wait_or_flag(&sm.mma2_done, (uint32_t)(c & 1), err, ok);
+            if (!named_bar_and(BAR_EY, 256, got)) {
+                ok = false;
+                break;
+            }
+            fence_after_sync();
+            {
+                uint32_t r[32];
+                tmem_ld32_async(la + D_YU + 32u * th, r);
                 tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) y[32 + j] = __uint_as_float(r[j]);
+                for (int j = 0; j < 32; ++j) y[j] = fmaf(sm.eg[32 * th + j], y[j], __uint_as_float(r[j]));
             }
             fence_before_sync();
-            mbar_arrive(&sm.y_free[c & 1]);
-            // sum over this warp's 32 v of y^2 for each of the 64 tokens: halving butterfly,
-            // lane L ends with tokens 2L and 2L+1
-            float a[C];
+            mbar_arrive(&sm.yu_free);
+            const int64_t t0 = (int64_t)c * C + 32 * th;
+            const int n = (int)(T - t0 < 32 ? (T - t0 < 0 ? 0 : T - t0) : 32);
+            // sum over this warp's 32 v of y^2 per token: lane L ends with token 32 th + L
+            float a[16];
+            {
+                const bool up = (lane & 16) != 0;
 #pragma unroll
-            for (int j = 0; j < C; ++j) a[j] = y[j] * y[j];
-            bfly_reduce<64, 16>(a, lane);
-            bfly_reduce<32, 8>(a, lane);
-            bfly_reduce<16, 4>(a, lane);
-            bfly_reduce<8, 2>(a, lane);
-            bfly_reduce<4, 1>(a, lane);
-            sm.red[ew][2 * lane] = a[0];
-            sm.red[ew][2 * lane + 1] = a[1];
-            tc::named_bar_sync(1, 128);
-            if (ew < 2) {
-                const int t = 32 * ew + lane;
-                const float ss = (sm.red[0][t] + sm.red[1][t]) + (sm.red[2][t] + sm.red[3][t]);
-                sm.inv[t] = 1.0f / sqrtf(ss / (float)D + 1e-6f);
+                for (int j = 0; j < 16; ++j) {
+                    const float lo2 = y[j] * y[j], hi2 = y[j + 16] * y[j + 16];
+                    a[j] = (up ? hi2 : lo2) + __shfl_xor_sync(0xffffffffu, up ? lo2 : hi2, 16);
+                }
             }
-            tc::named_bar_sync(1, 128);
-            const bool zok = wait_or_flag(&sm.full_z, (uint32_t)(c & 1), err, ok);
-            const int64_t t0 = (int64_t)c * C;
-            const int n = (int)(T - t0 < C ? T - t0 : C);
-            if (zok) {
+            bfly_reduce<16, 8>(a, lane);
+            bfly_reduce<8, 4>(a, lane);
+            bfly_reduce<4, 2>(a, lane);
+            bfly_reduce<2, 1>(a, lane);
+            sm.red[q4][32 * th + lane] = a[0];
+            tc::named_bar_sync(BAR_EY, 256);
+            const int tt = 32 * th + lane;
+            const float inv_l = 1.0f / sqrtf(((sm.red[0][tt] + sm.red[1][tt]) + (sm.red[2][tt] + sm.red[3][tt])) /
+                                                 (float)D + 1e-6f);
+            float zz[32];
 #pragma unroll
-                for (int t = 0; t < C; ++t)
-                    if (t < n)
-                        yb[(size_t)(t0 + t) * vc * D] = ((y[t] * sm.inv[t]) * wv) * siluf_acc(sm.zt[t][v]);
+            for (int j = 0; j < 32; ++j) zz[j] = j < n ? __ldg(zb + (size_t)(t0 + j) * INNER) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float inv = __shfl_sync(0xffffffffu, inv_l, j);
+                if (j < n) yb[(size_t)(t0 + j) * vc * D] = ((y[j] * inv) * wv) * silu_fast(zz[j]);
             }
-            mbar_arrive(&sm.z_free);
         }
     }
     fence_before_sync();
     __syncthreads();
-    if (warp == CTL_W) tmem_dealloc(tmem, 512);
+    if (warp == MMA_W) tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -827,18 +918,6 @@ bool make_split_map(CUtensorMap* m, const void* base, int64_t Tp, int heads) {
     cuuint32_t estr[4] = {1, 1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-// z [T][6144] f32 with (128 x 64) boxes, no swizzle; rows past T read as zero
-bool make_z_map(CUtensorMap* m, const float* z, int64_t T) {
-    EncodeTiledFn fn = tensor_map_encoder();
-    if (!fn) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)INNER, (cuuint64_t)T};
-    cuuint64_t strides[1] = {(cuuint64_t)INNER * 4};
-    cuuint32_t box[2] = {(cuuint32_t)SSM_D, (cuuint32_t)gp::C};
-    cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(z), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -868,9 +947,9 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
     float* bt = reinterpret_cast<float*>(base + 2 * qk_bytes + v_bytes + g_bytes);
     unsigned char* rec = base + 2 * qk_bytes + v_bytes + 2 * g_bytes;
 
-    CUtensorMap mq, mk, mv, mz;
+    CUtensorMap mq, mk, mv;
     if (!make_split_map(&mq, qs, Tp, SSM_HK) || !make_split_map(&mk, ks, Tp, SSM_HK) ||
-        !make_split_map(&mv, vs, Tp, vc) || !make_z_map(&mz, z, T))
+        !make_split_map(&mv, vs, Tp, vc))
         return cudaErrorInvalidValue;
 
     gdn_pf_prep_kernel<<<(unsigned)Tp, 256, 0, st>>>(T, Tp, vh0, vc, h0, qkv, slot.hist, L.conv_w, L.ssm_a,
@@ -879,11 +958,13 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
     const int smem_i = (int)sizeof(IntraSmem) + 1024;
     e = cudaFuncSetAttribute(gdn_pf_intra_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_i);
     if (e != cudaSuccess) return e;
-    gdn_pf_intra_kernel<<<dim3(NC, vc), 256, smem_i, st>>>(mq, mk, mv, Tp, vh0, vc, gl, bt, rec, ctx->d_err);
+    const int n_items = NC * vc;
+    gdn_pf_intra_kernel<<<std::min(n_items, ctx->n_sm), 256, smem_i, st>>>(mq, mk, mv, Tp, n_items, vh0, vc, gl, bt,
+                                                                          rec, ctx->d_err);
     const int smem_c = (int)sizeof(ChainSmem) + 1024;
     e = cudaFuncSetAttribute(gdn_pf_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_c);
     if (e != cudaSuccess) return e;
-    gdn_pf_chain_kernel<<<vc, CHAIN_THREADS, smem_c, st>>>(mq, mk, mz, T, NC, vh0, vc, rec, slot.state, L.norm_w, y,
+    gdn_pf_chain_kernel<<<vc, CHAIN_THREADS, smem_c, st>>>(mq, mk, T, NC, vh0, vc, rec, slot.state, z, L.norm_w, y,
                                                            ctx->d_err);
     *n_launch += 4;
     return cudaGetLastError();
