@@ -492,7 +492,9 @@ __global__ void __launch_bounds__(256, 1) gdn_pf_intra_kernel(const __grid_const
 namespace gp {
 struct alignas(1024) ChainSmem {
     // B operand of the S product, per chunk parity: [hi|lo][k-box][128 rows][64 k],
-    // rows 0-63 = Q of the chunk (TMA), rows 64-127 = W (record)
+    // rows 0-63 = Q of the chunk (TMA), rows 64-127 = W (record).  Once the S product
+    // of the chunk is done the buffer stages the chunk's z rows (TMA load, first 32 KB)
+    // and its y rows (TMA store, last 32 KB), f32 [64 t][128 v] each.
     unsigned char wq[2][65536];
     // B operand of the state update, per chunk parity: K [hi|lo][d-box][64 t][64 d]
     // (TMA), scaled in place by e^{G_last - G_t}
@@ -501,7 +503,7 @@ struct alignas(1024) ChainSmem {
     float gring[8][C];           // G of chunks c % 8
     float eg[C];                 // e^{G_t} of the chunk in the y epilogue
     float red[4][C];             // per-warp partial sums of y^2 per token
-    uint64_t full_wq[2], full_k[2], full_p, full_g[8];
+    uint64_t full_wq[2], full_k[2], full_p, full_g[8], full_z[2], wq_free[2];
     uint64_t mma1_done[2], mma3_done[2], mma2_done;
     uint64_t s_ready, u_ready, kd_ready[2], yp_free, yu_free;
     uint32_t tmem_base;
@@ -561,9 +563,9 @@ __device__ __forceinline__ void load_u0(const unsigned char* rec_u0, int v, int 
 }
 
 __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
-    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, int64_t T, int NC, int vh0,
-    int vc, const unsigned char* __restrict__ rec, float* __restrict__ state, const float* __restrict__ z,
-    const float* __restrict__ norm_w, float* __restrict__ y_out, int* err) {
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_y, int64_t T, int NC, int vh0,
+    int vc, const unsigned char* __restrict__ rec, float* __restrict__ state, const float* __restrict__ norm_w, int* err) {
     using namespace gp;
     using namespace tc;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -588,6 +590,10 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
         mbar_init(&sm.s_ready, 256);
         mbar_init(&sm.u_ready, 256);
         mbar_init(&sm.yp_free, 256);
+        mbar_init(&sm.full_z[0], 1);
+        mbar_init(&sm.full_z[1], 1);
+        mbar_init(&sm.wq_free[0], 1);
+        mbar_init(&sm.wq_free[1], 1);
         mbar_init(&sm.yu_free, 256);
         fence_mbar_init();
     }
@@ -619,13 +625,22 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
                 for (int hl = 0; hl < 2; ++hl)
                     for (int db = 0; db < 2; ++db)
                         tma_load_4d(sm.kd[b] + hl * 16384 + db * 8192, &tm_k, 64 * db, t0, hl, kh, &sm.full_k[b]);
-                // Q(c) and W(c) -> WQ[b]
-                if (c > 1 && !wait_or_flag(&sm.mma1_done[b], pp2, err, ok)) break;
+                // z(c-1) -> WQ[(c-1)%2] once the S product of chunk c-1 is done
+                if (c > 0) {
+                    const int bp = (c - 1) & 1;
+                    if (!wait_or_flag(&sm.mma1_done[bp], (uint32_t)(((c - 1) >> 1) & 1), err, ok)) break;
+                    mbar_arrive_expect_tx(&sm.full_z[bp], C * D * 4);
+                    tma_load_2d(sm.wq[bp], &tm_z, (vh0 + vl) * D, (c - 1) * C, &sm.full_z[bp]);
+                }
+                // G(c+5) into the slot of chunk c-3, whose last reader (the y epilogue) was done
+                // before MMA1(c-2)
                 if (c + 5 < NC) {
                     const int s = (c + 5) & 7;
                     mbar_arrive_expect_tx(&sm.full_g[s], 256);
                     bulk_g2s(sm.gring[s], R(c + 5) + REC_G, 256, &sm.full_g[s]);
                 }
+                // Q(c) and W(c) -> WQ[b] once the y rows of chunk c-2 have left it
+                if (c > 1 && !wait_or_flag(&sm.wq_free[b], pp2, err, ok)) break;
                 mbar_arrive_expect_tx(&sm.full_wq[b], 65536);
                 for (int hl = 0; hl < 2; ++hl)
                     for (int kb = 0; kb < 2; ++kb) {
@@ -637,6 +652,14 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
                 if (c > 0 && !wait_or_flag(&sm.mma2_done, (uint32_t)((c - 1) & 1), err, ok)) break;
                 mbar_arrive_expect_tx(&sm.full_p, 16384);
                 bulk_g2s(sm.p, R(c) + REC_P, 16384, &sm.full_p);
+            }
+            // z of the last chunk
+            if (ok && NC > 0) {
+                const int bp = (NC - 1) & 1;
+                if (wait_or_flag(&sm.mma1_done[bp], (uint32_t)(((NC - 1) >> 1) & 1), err, ok)) {
+                    mbar_arrive_expect_tx(&sm.full_z[bp], C * D * 4);
+                    tma_load_2d(sm.wq[bp], &tm_z, (vh0 + vl) * D, (NC - 1) * C, &sm.full_z[bp]);
+                }
             }
         }
     } else if (warp == MMA_W) {
@@ -830,8 +853,6 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
         const int v = 32 * q4 + lane;
         const uint32_t la = tmem + ((uint32_t)(32 * q4) << 16);
         const float wv = norm_w[v];
-        const float* zb = z + (size_t)(vh0 + vl) * D + v;
-        float* yb = y_out + (size_t)vl * D + v;
         for (int c = 0; c < NC; ++c) {
             const int b = c & 1, s = c & 7;
             // S Q^T of the chunk, as soon as the S product is done
@@ -868,8 +889,6 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
             }
             fence_before_sync();
             mbar_arrive(&sm.yu_free);
-            const int64_t t0 = (int64_t)c * C + 32 * th;
-            const int n = (int)(T - t0 < 32 ? (T - t0 < 0 ? 0 : T - t0) : 32);
             // sum over this warp's 32 v of y^2 per token: lane L ends with token 32 th + L
             float a[16];
             {
@@ -889,13 +908,28 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
             const int tt = 32 * th + lane;
             const float inv_l = 1.0f / sqrtf(((sm.red[0][tt] + sm.red[1][tt]) + (sm.red[2][tt] + sm.red[3][tt])) /
                                                  (float)D + 1e-6f);
-            float zz[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) zz[j] = j < n ? __ldg(zb + (size_t)(t0 + j) * INNER) : 0.0f;
+            // z rows of the chunk in WQ[b] (TMA, zero past T); y rows staged behind them
+            got = ok && wait_or_flag(&sm.full_z[b], (uint32_t)((c >> 1) & 1), err, ok);
+            if (!named_bar_and(BAR_EY, 256, got)) {
+                ok = false;
+                break;
+            }
+            const float* zt = reinterpret_cast<const float*>(sm.wq[b]);
+            float* yt = reinterpret_cast<float*>(sm.wq[b] + 32768);
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
+                const int t = 32 * th + j;
                 const float inv = __shfl_sync(0xffffffffu, inv_l, j);
-                if (j < n) yb[(size_t)(t0 + j) * vc * D] = ((y[j] * inv) * wv) * silu_fast(zz[j]);
+                yt[t * D + v] = ((y[j] * inv) * wv) * silu_fast(zt[t * D + v]);
+            }
+            fence_proxy_async_smem();
+            tc::named_bar_sync(BAR_EY, 256);
+            if (tid == 0) {
+                // rows past T are clipped by the tensor store
+                tma_store_2d(&tm_y, vl * D, c * C, yt);
+                bulk_commit();
+                bulk_wait_read_all();
+                mbar_arrive(&sm.wq_free[b]);
             }
         }
     }
@@ -918,6 +952,19 @@ bool make_split_map(CUtensorMap* m, const void* base, int64_t Tp, int heads) {
     cuuint32_t estr[4] = {1, 1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// f32 [rows][cols] with (128 x 64) boxes, no swizzle: the z rows of a head and
+// chunk (TMA load, zero past the last row) and the y rows (TMA store, clipped)
+bool make_rows_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols) {
+    EncodeTiledFn fn = tensor_map_encoder();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+    cuuint32_t box[2] = {(cuuint32_t)SSM_D, (cuuint32_t)gp::C};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -947,9 +994,9 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
     float* bt = reinterpret_cast<float*>(base + 2 * qk_bytes + v_bytes + g_bytes);
     unsigned char* rec = base + 2 * qk_bytes + v_bytes + 2 * g_bytes;
 
-    CUtensorMap mq, mk, mv;
+    CUtensorMap mq, mk, mv, mz, my;
     if (!make_split_map(&mq, qs, Tp, SSM_HK) || !make_split_map(&mk, ks, Tp, SSM_HK) ||
-        !make_split_map(&mv, vs, Tp, vc))
+        !make_split_map(&mv, vs, Tp, vc) || !make_rows_map(&mz, z, T, INNER) || !make_rows_map(&my, y, T, (int64_t)vc * D))
         return cudaErrorInvalidValue;
 
     gdn_pf_prep_kernel<<<(unsigned)Tp, 256, 0, st>>>(T, Tp, vh0, vc, h0, qkv, slot.hist, L.conv_w, L.ssm_a,
@@ -964,7 +1011,7 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
     const int smem_c = (int)sizeof(ChainSmem) + 1024;
     e = cudaFuncSetAttribute(gdn_pf_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_c);
     if (e != cudaSuccess) return e;
-    gdn_pf_chain_kernel<<<vc, CHAIN_THREADS, smem_c, st>>>(mq, mk, T, NC, vh0, vc, rec, slot.state, z, L.norm_w, y,
+    gdn_pf_chain_kernel<<<vc, CHAIN_THREADS, smem_c, st>>>(mq, mk, mz, my, T, NC, vh0, vc, rec, slot.state, L.norm_w,
                                                            ctx->d_err);
     *n_launch += 4;
     return cudaGetLastError();
