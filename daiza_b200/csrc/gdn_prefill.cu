@@ -56,7 +56,7 @@ constexpr uint32_t REC_BYTES = 81920 + 256;
 }  // namespace gp
 
 // ---------------------------------------------------------------------------
-// Phase A: conv1d + SiLU + L2 norms + gates, one CTA per (padded) token
+// Phase A: conv1d + SiLU + L2 norms + gates, one CTA per 4 (padded) tokens
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void store_split4(__nv_bfloat16* hi_row, size_t lo_offset, int lane, float4 x) {
     uint32_t h01, l01, h23, l23;
@@ -65,6 +65,8 @@ __device__ __forceinline__ void store_split4(__nv_bfloat16* hi_row, size_t lo_of
     *reinterpret_cast<uint2*>(hi_row + 4 * lane) = make_uint2(h01, h23);
     *reinterpret_cast<uint2*>(hi_row + lo_offset + 4 * lane) = make_uint2(l01, l23);
 }
+
+constexpr int PREP_TOK = 4;      // tokens per prep CTA: conv weights and shared input rows are read once for 4 tokens
 
 __global__ void __launch_bounds__(256) gdn_pf_prep_kernel(int64_t T, int64_t Tp, int vh0, int vc, int h0,
                                                           const float* __restrict__ qkv,
@@ -77,8 +79,7 @@ __global__ void __launch_bounds__(256) gdn_pf_prep_kernel(int64_t T, int64_t Tp,
                                                           __nv_bfloat16* __restrict__ qs, __nv_bfloat16* __restrict__ ks,
                                                           __nv_bfloat16* __restrict__ vs, float* __restrict__ gl,
                                                           float* __restrict__ bt) {
-    const int64_t t = blockIdx.x;
-    const bool pad = t >= T;     // rows of the last chunk past T: zero operands, g = 0, beta = 0
+    const int64_t tb = (int64_t)blockIdx.x * PREP_TOK;   // first token of this CTA (Tp is a multiple of 4)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float qscale = 1.0f / sqrtf((float)SSM_D);
     const size_t lo_off = (size_t)Tp * SSM_D;
@@ -87,41 +88,58 @@ __global__ void __launch_bounds__(256) gdn_pf_prep_kernel(int64_t T, int64_t Tp,
         __nv_bfloat16* dst;
         if (gi < SSM_HK) {                              // q head
             cb = gi * SSM_D;
-            dst = qs + ((size_t)gi * 2 * Tp + t) * SSM_D;
+            dst = qs + ((size_t)gi * 2 * Tp + tb) * SSM_D;
         } else if (gi < 2 * SSM_HK) {                   // k head
             cb = QKD + (gi - SSM_HK) * SSM_D;
-            dst = ks + ((size_t)(gi - SSM_HK) * 2 * Tp + t) * SSM_D;
+            dst = ks + ((size_t)(gi - SSM_HK) * 2 * Tp + tb) * SSM_D;
         } else {                                        // local v head
             cb = 2 * QKD + (vh0 + gi - 2 * SSM_HK) * SSM_D;
-            dst = vs + ((size_t)(gi - 2 * SSM_HK) * 2 * Tp + t) * SSM_D;
+            dst = vs + ((size_t)(gi - 2 * SSM_HK) * 2 * Tp + tb) * SSM_D;
         }
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (!pad) {
-            const int ch = cb + 4 * lane;
+        const int ch = cb + 4 * lane;
+        // input rows tb-3 .. tb+3 (ring slots (h0+t+ct+1)%4 before the batch; the reference's
+        // tap order: t=0 oldest ... t=3 the token itself), weights of the 4 taps
+        float4 x[PREP_TOK + CONV_K - 1], w[CONV_K];
 #pragma unroll
-            for (int ct = 0; ct < CONV_K; ++ct) {
-                const int64_t st = t + ct - (CONV_K - 1);
-                const float* src = st >= 0 ? qkv + st * QKV_LEN
-                                           : hist + (size_t)((h0 + t + ct + 1) % CONV_K) * QKV_LEN;
-                const float4 x = *reinterpret_cast<const float4*>(src + ch);
-                const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)ct * QKV_LEN + ch);
-                acc.x = fmaf(x.x, w.x, acc.x);
-                acc.y = fmaf(x.y, w.y, acc.y);
-                acc.z = fmaf(x.z, w.z, acc.z);
-                acc.w = fmaf(x.w, w.w, acc.w);
+        for (int ct = 0; ct < CONV_K; ++ct) w[ct] = *reinterpret_cast<const float4*>(conv_w + (size_t)ct * QKV_LEN + ch);
+#pragma unroll
+        for (int r = 0; r < PREP_TOK + CONV_K - 1; ++r) {
+            const int64_t st = tb + r - (CONV_K - 1);
+            const float* src;
+            if (st >= T) src = nullptr;
+            else if (st >= 0) src = qkv + st * QKV_LEN;
+            else src = hist + (size_t)((h0 + st + CONV_K) % CONV_K) * QKV_LEN;
+            x[r] = src ? *reinterpret_cast<const float4*>(src + ch) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < PREP_TOK; ++k) {
+            const int64_t t = tb + k;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t < T) {                                // rows of the last chunk past T stay zero
+#pragma unroll
+                for (int ct = 0; ct < CONV_K; ++ct) {
+                    const float4 xv = x[k + ct];
+                    acc.x = fmaf(xv.x, w[ct].x, acc.x);
+                    acc.y = fmaf(xv.y, w[ct].y, acc.y);
+                    acc.z = fmaf(xv.z, w[ct].z, acc.z);
+                    acc.w = fmaf(xv.w, w[ct].w, acc.w);
+                }
+                acc = make_float4(siluf_acc(acc.x), siluf_acc(acc.y), siluf_acc(acc.z), siluf_acc(acc.w));
             }
-            acc = make_float4(siluf_acc(acc.x), siluf_acc(acc.y), siluf_acc(acc.z), siluf_acc(acc.w));
-            if (gi < 2 * SSM_HK) {
+            if (gi < 2 * SSM_HK) {                      // warp-uniform branch: every lane reaches the shuffles
                 const float ss = warp_sum(acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w);
                 const float inv = 1.0f / sqrtf(ss + 1e-6f);
                 acc = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
                 if (gi < SSM_HK) acc = make_float4(acc.x * qscale, acc.y * qscale, acc.z * qscale, acc.w * qscale);
             }
+            store_split4(dst + (size_t)k * SSM_D, lo_off, lane, acc);
         }
-        store_split4(dst, lo_off, lane, acc);
     }
-    for (int vl = threadIdx.x; vl < vc; vl += blockDim.x) {
+    for (int i = threadIdx.x; i < vc * PREP_TOK; i += blockDim.x) {
+        const int vl = i % vc, k = i / vc;
+        const int64_t t = tb + k;
         const int vh = vh0 + vl;
+        const bool pad = t >= T;     // g = 0, beta = 0 past T
         gl[(size_t)vl * Tp + t] = pad ? 0.0f : ssm_a[vh] * softplus_ref(alpha[(size_t)t * SSM_HV + vh] + dt_bias[vh]);
         bt[(size_t)vl * Tp + t] = pad ? 0.0f : sigmoidf_acc(beta[(size_t)t * SSM_HV + vh]);
     }
@@ -999,8 +1017,8 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
         !make_split_map(&mv, vs, Tp, vc) || !make_rows_map(&mz, z, T, INNER) || !make_rows_map(&my, y, T, (int64_t)vc * D))
         return cudaErrorInvalidValue;
 
-    gdn_pf_prep_kernel<<<(unsigned)Tp, 256, 0, st>>>(T, Tp, vh0, vc, h0, qkv, slot.hist, L.conv_w, L.ssm_a,
-                                                     L.dt_bias, alpha, beta, qs, ks, vs, gl, bt);
+    gdn_pf_prep_kernel<<<(unsigned)(Tp / PREP_TOK), 256, 0, st>>>(T, Tp, vh0, vc, h0, qkv, slot.hist, L.conv_w, L.ssm_a,
+                                                                  L.dt_bias, alpha, beta, qs, ks, vs, gl, bt);
     gdn_pf_ring_kernel<<<(unsigned)(T < CONV_K ? T : CONV_K), 256, 0, st>>>(T, h0, qkv, slot.hist);
     const int smem_i = (int)sizeof(IntraSmem) + 1024;
     e = cudaFuncSetAttribute(gdn_pf_intra_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_i);
