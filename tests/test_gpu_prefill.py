@@ -108,8 +108,8 @@ def test_gqa_prefill_head_slice():
 
 
 def test_gqa_prefill_full_8192_sampled_rows():
-    """Config 3 size (T=8192, positions 0..8191): sampled query rows against the
-    oracle (rows spread over every 128-row tile boundary class), every cache row."""
+    """Config 3 size (T=8192, positions 0..8191): about 256 query rows spanning every
+    128-row tile against the oracle, and every cache row."""
     seed = O.SEED0 + 3
     T = 8192
     ctx, qn, kn = make_ctx([T], seed)
@@ -121,10 +121,15 @@ def test_gqa_prefill_full_8192_sampled_rows():
     out = torch.empty(T, 6144, device="cuda")
     ctx.gqa_prefill(1, 0, qg, k, v, out)
     torch.cuda.synchronize()
-    rows = np.array([0, 1, 63, 64, 127, 128, 1000, 4095, 4096, 6143, 8127, 8128, 8190, 8191])
+    # 256 rows: the first and last row of every 128-row query tile plus two more per tile
+    rng = np.random.default_rng(seed)
+    rows = np.unique(np.concatenate([np.arange(0, T, 128), np.arange(127, T, 128),
+                                     np.arange(0, T, 128) + rng.integers(1, 127, T // 128),
+                                     np.arange(0, T, 128) + rng.integers(1, 127, T // 128)]))
+    assert rows.size >= 250 and np.array_equal(np.unique(rows // 128), np.arange(T // 128))
     kv = O.OracleKv(T)
     want = O.gqa_prefill_rows(qg.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
-                              qn, kn, kv, rows, n_threads=16)
+                              qn, kn, kv, rows, n_threads=32)
     got = out.cpu().numpy()[rows]
     assert_close(got, want, TOL_BF16, "sampled rows")
     ke, ve = ctx.kv_export(1, 0)
