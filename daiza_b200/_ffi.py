@@ -53,6 +53,9 @@ SIGNATURES = {
     "dz_rope_table": [_P, _I64, _I64, _P],
     "dz_kv_fill_pattern": [_P, _I, _I, _I64, _I],
     "dz_gqa_decode": [_P, _I, _I, _P, _P, _P, _P, _P, _P],
+    "dz_gqa_decode_at": [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P],
+    "dz_gqa_prefill_bf16_at": [_P, _I, _I, _I64, _I64, _P, _P, _P, _P, _P],
+    "dz_gqa_prefill_at": [_P, _I, _I, _I64, _I64, _P, _P, _P, _P, _P],
     "dz_gdn_decode": [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P],
     "dz_gqa_prefill_bf16": [_P, _I, _I, _I64, _P, _P, _P, _P, _P],
     "dz_gqa_prefill": [_P, _I, _I, _I64, _P, _P, _P, _P, _P],

@@ -35,19 +35,6 @@ dz_status cuda_fail(dz_ctx* ctx, cudaError_t e, const char* what) {
         if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call);      \
     } while (0)
 
-struct DeviceGuard {
-    int prev = -1;
-    explicit DeviceGuard(int dev) {
-        cudaGetDevice(&prev);
-        if (prev != dev) cudaSetDevice(dev);
-    }
-    ~DeviceGuard() {
-        int cur;
-        cudaGetDevice(&cur);
-        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-    }
-};
-
 bool layer_ok(const dz_ctx* ctx, int layer) { return ctx && layer >= 0 && layer < (int)ctx->layers.size(); }
 
 void free_cache(dz_ctx* ctx) {
@@ -509,8 +496,9 @@ dz_status dz_rope_table(dz_ctx* ctx, int64_t pos0, int64_t n, float* out) {
 // ---------------------------------------------------------------------------
 // decode
 // ---------------------------------------------------------------------------
-static dz_status gqa_decode_impl(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* q_gate,
-                                 const float* k, const float* v, float* out, cudaStream_t st) {
+// pos: host RoPE positions [B] (ModelState::pos), or null for pos = len
+static dz_status gqa_decode_impl(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const int32_t* pos,
+                                 const float* q_gate, const float* k, const float* v, float* out, cudaStream_t st) {
     LayerState& L = ctx->layers[layer];
     const int kvc = ctx->cfg.kv_head_count;
     const int nq = GRP * kvc;
@@ -519,25 +507,20 @@ static dz_status gqa_decode_impl(dz_ctx* ctx, int layer, int B, const int32_t* s
         const int nb = std::min(MAXB, B - b0);
         GqaDecodeDesc d;
         d.B = nb;
-        // split-K chunk (positions per warp work item): ~4 items per resident warp
-        // (4 warps per SM) over the whole batch, 16..1024 positions, at most MAXC
-        // chunks per (sequence, kv head)
         int64_t total = 0, nmax = 0;
         for (int b = 0; b < nb; ++b) {
             const int64_t n = L.len[seq_ids[b0 + b]] + 1;
             total += n;
             nmax = std::max(nmax, n);
         }
-        int64_t chunk = (total * kvc) / ((int64_t)ctx->n_sm * 16);
-        chunk = std::min<int64_t>(std::max<int64_t>(chunk, 16), 1024);
-        chunk = std::max<int64_t>(chunk, (nmax + MAXC - 1) / MAXC);
-        chunk = (chunk + 15) / 16 * 16;
+        const int64_t chunk = decode_chunk(ctx->n_sm, kvc, total, nmax);
         d.chunk = (int)chunk;
         d.cum[0] = 0;
         for (int b = 0; b < nb; ++b) {
             const int s = seq_ids[b0 + b];
             d.sid[b] = s;
             d.len[b] = (int32_t)L.len[s];
+            d.pos[b] = pos ? pos[b0 + b] : (int32_t)L.len[s];
             d.cum[b + 1] = d.cum[b] + (int32_t)((L.len[s] + 1 + chunk - 1) / chunk);
         }
         cudaError_t e = launch_gqa_decode(ctx, layer, d, q_gate + (size_t)b0 * nq * QG_ROW, k + (size_t)b0 * kvc * HD,
@@ -549,13 +532,19 @@ static dz_status gqa_decode_impl(dz_ctx* ctx, int layer, int B, const int32_t* s
     return DZ_OK;
 }
 
-static dz_status gqa_decode_check(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids) {
+static dz_status gqa_decode_check(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids,
+                                  const int32_t* pos = nullptr) {
     if (!layer_ok(ctx, layer)) return fail(ctx, DZ_EINVAL, "bad layer %d", layer);
     const LayerState& L = ctx->layers[layer];
     if (!L.is_attn) return fail(ctx, DZ_EINVAL, "layer %d is not a full-attention layer", layer);
     if (!L.params_set) return fail(ctx, DZ_ESTATE, "layer %d has no parameters", layer);
     dz_status st = check_seqs(ctx, B, seq_ids);
     if (st != DZ_OK) return st;
+    if (pos)
+        for (int b = 0; b < B; ++b)
+            if (pos[b] < 0 || pos[b] >= ctx->rope_n)
+                return fail(ctx, DZ_EINVAL, "pos[%d]=%d outside the RoPE table [0, %lld)", b, pos[b],
+                            (long long)ctx->rope_n);
     for (int b = 0; b < B; ++b)
         if (L.len[seq_ids[b]] + 1 > L.h_kv[seq_ids[b]].cap)
             return fail(ctx, DZ_ESTATE, "KV cache of seq %d is full (cap %lld)", seq_ids[b],
@@ -569,7 +558,18 @@ dz_status dz_gqa_decode(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, c
     if (st != DZ_OK) return st;
     if (!q_gate || !k || !v || !out) return fail(ctx, DZ_EINVAL, "null tensor");
     DeviceGuard g(ctx->device);
-    return gqa_decode_impl(ctx, layer, B, seq_ids, q_gate, k, v, out, static_cast<cudaStream_t>(stream));
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    return gqa_decode_impl(ctx, layer, B, seq_ids, nullptr, q_gate, k, v, out, static_cast<cudaStream_t>(stream));
+}
+
+dz_status dz_gqa_decode_at(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const int32_t* pos,
+                           const float* q_gate, const float* k, const float* v, float* out, void* stream) {
+    dz_status st = gqa_decode_check(ctx, layer, B, seq_ids, pos);
+    if (st != DZ_OK) return st;
+    if (!q_gate || !k || !v || !out) return fail(ctx, DZ_EINVAL, "null tensor");
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    return gqa_decode_impl(ctx, layer, B, seq_ids, pos, q_gate, k, v, out, static_cast<cudaStream_t>(stream));
 }
 
 dz_status dz_gqa_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* q_gate,
@@ -589,7 +589,7 @@ dz_status dz_gqa_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_i
     DZ_CUDA(cudaMemcpyAsync(dq, q_gate, nqg * 4, cudaMemcpyHostToDevice, s));
     DZ_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, s));
     DZ_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, s));
-    if ((st = gqa_decode_impl(ctx, layer, B, seq_ids, dq, dk, dv, dout, s)) != DZ_OK) return st;
+    if ((st = gqa_decode_impl(ctx, layer, B, seq_ids, nullptr, dq, dk, dv, dout, s)) != DZ_OK) return st;
     DZ_CUDA(cudaMemcpyAsync(out, dout, no * 4, cudaMemcpyDeviceToHost, s));
     DZ_CUDA(cudaStreamSynchronize(s));
     return DZ_OK;
@@ -663,9 +663,10 @@ dz_status dz_gdn_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_i
 // ---------------------------------------------------------------------------
 // prefill
 // ---------------------------------------------------------------------------
-static dz_status gqa_prefill_common(dz_ctx* ctx, int layer, int seq, int64_t T, const uint16_t* qg16,
-                                    const uint16_t* k16, const uint16_t* v16, const float* qgf, const float* kf,
-                                    const float* vf, float* out, void* stream) {
+// start_pos: RoPE position of the first token (forward.rs:550-557), < 0 for the cache length
+static dz_status gqa_prefill_common(dz_ctx* ctx, int layer, int seq, int64_t T, int64_t start_pos,
+                                    const uint16_t* qg16, const uint16_t* k16, const uint16_t* v16, const float* qgf,
+                                    const float* kf, const float* vf, float* out, void* stream) {
     if (!layer_ok(ctx, layer)) return fail(ctx, DZ_EINVAL, "bad layer %d", layer);
     LayerState& L = ctx->layers[layer];
     if (!L.is_attn) return fail(ctx, DZ_EINVAL, "layer %d is not a full-attention layer", layer);
@@ -676,9 +677,14 @@ static dz_status gqa_prefill_common(dz_ctx* ctx, int layer, int seq, int64_t T, 
     if (L.len[seq] + T > L.h_kv[seq].cap)
         return fail(ctx, DZ_ESTATE, "prefill of %lld tokens overflows KV cache (len %lld, cap %lld)", (long long)T,
                     (long long)L.len[seq], (long long)L.h_kv[seq].cap);
+    const int64_t p0 = start_pos < 0 ? L.len[seq] : start_pos;
+    if (p0 + T > ctx->rope_n)
+        return fail(ctx, DZ_EINVAL, "positions [%lld, %lld) outside the RoPE table [0, %lld)", (long long)p0,
+                    (long long)(p0 + T), (long long)ctx->rope_n);
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     int launches = 0;
-    cudaError_t e = launch_gqa_prefill(ctx, layer, seq, T, qg16, k16, v16, qgf, kf, vf, out,
+    cudaError_t e = launch_gqa_prefill(ctx, layer, seq, T, p0, qg16, k16, v16, qgf, kf, vf, out,
                                        static_cast<cudaStream_t>(stream), &launches);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "gqa prefill launch");
     L.len[seq] += T;
@@ -689,13 +695,28 @@ static dz_status gqa_prefill_common(dz_ctx* ctx, int layer, int seq, int64_t T, 
 dz_status dz_gqa_prefill_bf16(dz_ctx* ctx, int layer, int seq, int64_t T, const uint16_t* q_gate, const uint16_t* k,
                               const uint16_t* v, float* out, void* stream) {
     if (!q_gate || !k || !v) return fail(ctx, DZ_EINVAL, "null tensor");
-    return gqa_prefill_common(ctx, layer, seq, T, q_gate, k, v, nullptr, nullptr, nullptr, out, stream);
+    return gqa_prefill_common(ctx, layer, seq, T, -1, q_gate, k, v, nullptr, nullptr, nullptr, out, stream);
+}
+
+dz_status dz_gqa_prefill_bf16_at(dz_ctx* ctx, int layer, int seq, int64_t start_pos, int64_t T,
+                                 const uint16_t* q_gate, const uint16_t* k, const uint16_t* v, float* out,
+                                 void* stream) {
+    if (!q_gate || !k || !v) return fail(ctx, DZ_EINVAL, "null tensor");
+    if (start_pos < 0) return fail(ctx, DZ_EINVAL, "start_pos must be non-negative");
+    return gqa_prefill_common(ctx, layer, seq, T, start_pos, q_gate, k, v, nullptr, nullptr, nullptr, out, stream);
 }
 
 dz_status dz_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* q_gate, const float* k,
                          const float* v, float* out, void* stream) {
     if (!q_gate || !k || !v) return fail(ctx, DZ_EINVAL, "null tensor");
-    return gqa_prefill_common(ctx, layer, seq, T, nullptr, nullptr, nullptr, q_gate, k, v, out, stream);
+    return gqa_prefill_common(ctx, layer, seq, T, -1, nullptr, nullptr, nullptr, q_gate, k, v, out, stream);
+}
+
+dz_status dz_gqa_prefill_at(dz_ctx* ctx, int layer, int seq, int64_t start_pos, int64_t T, const float* q_gate,
+                            const float* k, const float* v, float* out, void* stream) {
+    if (!q_gate || !k || !v) return fail(ctx, DZ_EINVAL, "null tensor");
+    if (start_pos < 0) return fail(ctx, DZ_EINVAL, "start_pos must be non-negative");
+    return gqa_prefill_common(ctx, layer, seq, T, start_pos, nullptr, nullptr, nullptr, q_gate, k, v, out, stream);
 }
 
 dz_status dz_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* qkv, const float* alpha,

@@ -26,7 +26,8 @@ struct GqaDecodeDesc {
     int B;
     int chunk;                 // positions per split-K chunk (multiple of 16)
     int32_t sid[MAXB];         // sequence slot of batch row b
-    int32_t len[MAXB];         // cache length before this token = slot = RoPE position
+    int32_t len[MAXB];         // cache length before this token = its slot
+    int32_t pos[MAXB];         // RoPE position of this token (= len unless the caller gives one)
     int32_t cum[MAXB + 1];     // prefix sum of chunks(b) = ceil((len+1)/chunk)
 };
 
@@ -85,13 +86,50 @@ struct dz_ctx {
 };
 
 namespace dz {
+// Positions per split-K work item of a GQA decode launch (shared by every decode
+// entry point so they split a batch the same way): ~4 items per resident warp
+// (4 warps per SM) over the whole batch, 16..1024 positions, at most MAXC chunks
+// per (sequence, kv head), a multiple of 16.  total / nmax: sum and max of
+// len + 1 over the batch.
+inline int64_t decode_chunk(int n_sm, int kvc, int64_t total, int64_t nmax) {
+    int64_t chunk = (total * kvc) / ((int64_t)n_sm * 16);
+    chunk = chunk < 16 ? 16 : (chunk > 1024 ? 1024 : chunk);
+    const int64_t need = (nmax + MAXC - 1) / MAXC;
+    if (chunk < need) chunk = need;
+    return (chunk + 15) / 16 * 16;
+}
+
+// Makes `dev` current for the lifetime of the guard and restores the caller's
+// device afterwards; `ok` is false if the switch failed.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) {
+            cudaGetLastError();
+            prev = -1;
+        }
+        if (prev != dev && cudaSetDevice(dev) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+        }
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
+
 // launchers (return cudaError_t of the last launch)
 cudaError_t launch_gqa_decode(dz_ctx* ctx, int layer, const GqaDecodeDesc& d, const float* q_gate,
                               const float* k, const float* v, float* out, cudaStream_t st, int* n_launch);
 cudaError_t launch_gdn_decode(dz_ctx* ctx, int layer, const GdnDecodeDesc& d, const float* qkv,
                               const float* alpha, const float* beta, const float* z, float* y,
                               cudaStream_t st, int* n_launch);
-cudaError_t launch_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const uint16_t* q_gate,
+// rope_pos0: RoPE position of the first token (the cache slots start at the current length)
+cudaError_t launch_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, int64_t rope_pos0, const uint16_t* q_gate,
                                const uint16_t* k, const uint16_t* v, const float* q_gate_f, const float* k_f,
                                const float* v_f, float* out, cudaStream_t st, int* n_launch);
 cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* qkv, const float* alpha,

@@ -39,10 +39,10 @@ __global__ void __launch_bounds__(256) gqa_prep_kernel(GqaDecodeDesc d, int kvc,
     const int b = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sid = d.sid[b];
-    const int pos = d.len[b];
+    const int pos = d.len[b];                      // cache slot (kv_cache.rs:79-88)
     const int nq = GRP * kvc;
     const KvSlot slot = kv[sid];
-    const float* cs = rope + (size_t)pos * (2 * ROPE);
+    const float* cs = rope + (size_t)d.pos[b] * (2 * ROPE);   // RoPE row of ModelState::pos (forward.rs:230-238)
     for (int task = warp; task < nq + kvc; task += 8) {
         const float* src;
         const float* w;

@@ -24,11 +24,20 @@
 // device, so two calls whose kernels overlap on the GPU (different streams, no
 // ordering between them) race on it; callers must order them.
 //
-// The array's device address is looked up once per device with
-// cudaGetSymbolAddress (host code must not use the symbol itself: on the host
-// it is only a stand-in, not a device address).  That lookup happens inside the
-// first call of this entry point on each device, so that first call should be
-// made before any stream capture begins.
+// The array's device address is looked up with cudaGetSymbolAddress (host code
+// must not use the symbol itself: on the host it is only a stand-in, not a
+// device address).  The lookup happens inside the first call of this entry
+// point on each device, so that first call should be made before any stream
+// capture begins.  The address is cached together with the device's current
+// context; if that context changes (a cudaDeviceReset in between), the next
+// call looks the address up again.
+//
+// The split-K chunk is the one dz_gqa_decode picks for the same batch, doubled
+// until the call needs at most DZ_NOALLOC_MAX_ITEMS work items; when no
+// doubling is needed both entry points split the batch identically and give
+// the same results bit for bit, otherwise they agree to f32 rounding.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "dz_internal.h"
@@ -50,6 +59,7 @@ constexpr int MAX_DEVICES = 64;
 
 std::mutex g_mu;
 float* g_scratch[MAX_DEVICES] = {};
+CUcontext g_scratch_ctx[MAX_DEVICES] = {};
 }  // namespace
 
 static __device__ __align__(256) float dz_noalloc_scratch[SCRATCH_FLOATS];
@@ -65,7 +75,20 @@ dz_status set_err(dz_ctx* ctx, dz_status st, const std::string& msg) {
 dz_status scratch_address(dz_ctx* ctx, int dev, float** out) {
     if (dev < 0 || dev >= MAX_DEVICES) return set_err(ctx, DZ_EINVAL, "device index out of range for no-alloc scratch");
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_scratch[dev]) {
+    // the current context's handle, through the driver entry point (the library
+    // has no link-time dependency on libcuda)
+    typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+    static CtxGetCurrentFn ctx_get_current = nullptr;
+    if (!ctx_get_current) {
+        void* fp = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fp, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fp);
+    }
+    CUcontext cur = nullptr;
+    if (!ctx_get_current || ctx_get_current(&cur) != CUDA_SUCCESS) cur = nullptr;
+    if (!g_scratch[dev] || cur != g_scratch_ctx[dev]) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, dz_noalloc_scratch);
         if (e != cudaSuccess || !p) {
@@ -74,6 +97,7 @@ dz_status scratch_address(dz_ctx* ctx, int dev, float** out) {
                                               cudaGetErrorString(e));
         }
         g_scratch[dev] = static_cast<float*>(p);
+        g_scratch_ctx[dev] = cur;
     }
     *out = g_scratch[dev];
     return DZ_OK;
@@ -114,10 +138,7 @@ extern "C" dz_status dz_gqa_decode_noalloc(dz_ctx* ctx, int layer, int B, const 
         total += n;
         nmax = std::max(nmax, n);
     }
-    int64_t chunk = (total * kvc) / ((int64_t)ctx->n_sm * 4);
-    chunk = std::min<int64_t>(std::max<int64_t>(chunk, 32), 1024);
-    chunk = std::max<int64_t>(chunk, (nmax + MAXC - 1) / MAXC);
-    chunk = (chunk + 15) / 16 * 16;
+    int64_t chunk = decode_chunk(ctx->n_sm, kvc, total, nmax);
     auto items_for = [&](int64_t c) {
         int64_t it = 0;
         for (int b = 0; b < B; ++b) it += (L.len[seq_ids[b]] + 1 + c - 1) / c;
@@ -130,12 +151,12 @@ extern "C" dz_status dz_gqa_decode_noalloc(dz_ctx* ctx, int layer, int B, const 
         const int s = seq_ids[b];
         d.sid[b] = s;
         d.len[b] = (int32_t)L.len[s];
+        d.pos[b] = (int32_t)L.len[s];
         d.cum[b + 1] = d.cum[b] + (int32_t)((L.len[s] + 1 + chunk - 1) / chunk);
     }
 
-    int prev = -1;
-    cudaGetDevice(&prev);
-    if (prev != ctx->device) cudaSetDevice(ctx->device);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return set_err(ctx, DZ_ECUDA, "cudaSetDevice failed");
     float* base = nullptr;
     dz_status st = scratch_address(ctx, ctx->device, &base);
     if (st == DZ_OK) {
@@ -149,6 +170,6 @@ extern "C" dz_status dz_gqa_decode_noalloc(dz_ctx* ctx, int layer, int B, const 
             ctx->last_launches = launches;
         }
     }
-    if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
     return st;
 }
+

@@ -228,7 +228,7 @@ __device__ __forceinline__ void st4_bf16(__nv_bfloat16* p, float4 x) {
 }
 
 template <typename Tin>
-__global__ void __launch_bounds__(256) pf_prep_kernel(int kvc, int64_t T, int64_t base, KvSlot slot,
+__global__ void __launch_bounds__(256) pf_prep_kernel(int kvc, int64_t T, int64_t base, int64_t rope_pos0, KvSlot slot,
                                                       const float* __restrict__ q_norm,
                                                       const float* __restrict__ k_norm,
                                                       const float* __restrict__ rope, const Tin* __restrict__ q_gate,
@@ -238,8 +238,8 @@ __global__ void __launch_bounds__(256) pf_prep_kernel(int kvc, int64_t T, int64_
     const int64_t t = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nq = GRP * kvc;
-    const int64_t pos = base + t;
-    const float* cs = rope + pos * (2 * ROPE);
+    const int64_t pos = base + t;                                   // cache slot
+    const float* cs = rope + (rope_pos0 + t) * (2 * ROPE);           // RoPE row of start_pos + t (forward.rs:550-557)
     for (int task = warp; task < nq + kvc; task += 8) {
         const Tin* src;
         const float* w;
@@ -601,7 +601,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t d1, int64_t d2, int box_
 
 }  // namespace
 
-cudaError_t launch_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const uint16_t* q_gate,
+cudaError_t launch_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, int64_t rope_pos0, const uint16_t* q_gate,
                                const uint16_t* k, const uint16_t* v, const float* q_gate_f, const float* k_f,
                                const float* v_f, float* out, cudaStream_t st, int* n_launch) {
     const LayerState& Lr = ctx->layers[layer];
@@ -618,11 +618,11 @@ cudaError_t launch_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
     const bool bf = q_gate != nullptr;
     if (bf)
         pf_prep_kernel<__nv_bfloat16><<<(unsigned)T, 256, 0, st>>>(
-            kvc, T, base, slot, Lr.q_norm, Lr.k_norm, ctx->rope, reinterpret_cast<const __nv_bfloat16*>(q_gate),
+            kvc, T, base, rope_pos0, slot, Lr.q_norm, Lr.k_norm, ctx->rope, reinterpret_cast<const __nv_bfloat16*>(q_gate),
             reinterpret_cast<const __nv_bfloat16*>(k), reinterpret_cast<const __nv_bfloat16*>(v), qb, kb, vb, L,
             ctx->cfg.rms_eps);
     else
-        pf_prep_kernel<float><<<(unsigned)T, 256, 0, st>>>(kvc, T, base, slot, Lr.q_norm, Lr.k_norm, ctx->rope,
+        pf_prep_kernel<float><<<(unsigned)T, 256, 0, st>>>(kvc, T, base, rope_pos0, slot, Lr.q_norm, Lr.k_norm, ctx->rope,
                                                           q_gate_f, k_f, v_f, qb, kb, vb, L, ctx->cfg.rms_eps);
     *n_launch += 1;
     if (base > 0) {

@@ -176,21 +176,35 @@ class Context:
         return SsmStateView(self, layer, seq)
 
     # ---- compute (device tensors) ------------------------------------------
-    def gqa_decode(self, layer, seq_ids, q_gate, k, v, out, stream=None):
+    def gqa_decode(self, layer, seq_ids, q_gate, k, v, out, stream=None, pos=None):
+        """pos: RoPE positions of the new tokens (ModelState::pos); default = cache lengths."""
         ids = np.ascontiguousarray(np.atleast_1d(seq_ids), np.int32)
-        self._chk(self.lib.dz_gqa_decode(self.h, layer, len(ids), _np_ptr(ids), _ptr(q_gate), _ptr(k), _ptr(v),
-                                         _ptr(out), _stream(stream)))
+        if pos is None:
+            self._chk(self.lib.dz_gqa_decode(self.h, layer, len(ids), _np_ptr(ids), _ptr(q_gate), _ptr(k), _ptr(v),
+                                             _ptr(out), _stream(stream)))
+            return
+        ps = np.ascontiguousarray(np.atleast_1d(pos), np.int32)
+        assert ps.shape == ids.shape
+        self._chk(self.lib.dz_gqa_decode_at(self.h, layer, len(ids), _np_ptr(ids), _np_ptr(ps), _ptr(q_gate), _ptr(k),
+                                            _ptr(v), _ptr(out), _stream(stream)))
 
     def gdn_decode(self, layer, seq_ids, qkv, alpha, beta, z, y, stream=None):
         ids = np.ascontiguousarray(np.atleast_1d(seq_ids), np.int32)
         self._chk(self.lib.dz_gdn_decode(self.h, layer, len(ids), _np_ptr(ids), _ptr(qkv), _ptr(alpha), _ptr(beta),
                                          _ptr(z), _ptr(y), _stream(stream)))
 
-    def gqa_prefill(self, layer, seq, q_gate, k, v, out, stream=None):
+    def gqa_prefill(self, layer, seq, q_gate, k, v, out, stream=None, start_pos=None):
+        """start_pos: RoPE position of the first token (forward.rs:550-557); default = cache length."""
         import torch
         T = q_gate.shape[0]
-        fn = self.lib.dz_gqa_prefill_bf16 if q_gate.dtype == torch.bfloat16 else self.lib.dz_gqa_prefill
-        self._chk(fn(self.h, layer, seq, T, _ptr(q_gate), _ptr(k), _ptr(v), _ptr(out), _stream(stream)))
+        bf = q_gate.dtype == torch.bfloat16
+        if start_pos is None:
+            fn = self.lib.dz_gqa_prefill_bf16 if bf else self.lib.dz_gqa_prefill
+            self._chk(fn(self.h, layer, seq, T, _ptr(q_gate), _ptr(k), _ptr(v), _ptr(out), _stream(stream)))
+            return
+        fn = self.lib.dz_gqa_prefill_bf16_at if bf else self.lib.dz_gqa_prefill_at
+        self._chk(fn(self.h, layer, seq, int(start_pos), T, _ptr(q_gate), _ptr(k), _ptr(v), _ptr(out),
+                     _stream(stream)))
 
     def gdn_prefill(self, layer, seq, qkv, alpha, beta, z, y, stream=None):
         T = qkv.shape[0]

@@ -130,6 +130,13 @@ dz_status dz_rope_table(dz_ctx* ctx, int64_t pos0, int64_t n, float* out);
  *   k, v   [B][kvc][256]     out [B][6*kvc][256]      (kvc = kv_head_count)  */
 dz_status dz_gqa_decode(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* q_gate,
                         const float* k, const float* v, float* out, void* stream);
+/* dz_gqa_decode with explicit RoPE positions: pos (host int32 [B]) is the position
+ * of each sequence's new token, as ModelState::pos feeds rope_cos_sin_mrope_text_into
+ * in the reference (model/forward.rs:230-238); the KV slot is still the cache
+ * length.  pos[b] must lie inside the RoPE table (dz_cache_create's largest
+ * capacity).  dz_gqa_decode is this call with pos = the cache lengths. */
+dz_status dz_gqa_decode_at(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const int32_t* pos,
+                           const float* q_gate, const float* k, const float* v, float* out, void* stream);
 /* Gated DeltaNet core of ssm_forward_into (model/ssm.rs:466-611): ring conv1d
  * + SiLU, L2-norm q/k, q *= 1/sqrt(128), gates, gated delta rule on the
  * [v][k] state, gated RMSNorm output.
@@ -147,6 +154,14 @@ dz_status dz_gqa_prefill_bf16(dz_ctx* ctx, int layer, int seq, int64_t T, const 
 /* Same with f32 inputs (converted on device). */
 dz_status dz_gqa_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* q_gate, const float* k,
                          const float* v, float* out, void* stream);
+/* The two prefills with an explicit RoPE start: token t is rotated at position
+ * start_pos + t (model/forward.rs:550-557, pos = start_pos + t) while its KV slot
+ * is len + t.  The plain entry points use start_pos = the cache length. */
+dz_status dz_gqa_prefill_bf16_at(dz_ctx* ctx, int layer, int seq, int64_t start_pos, int64_t T,
+                                 const uint16_t* q_gate, const uint16_t* k, const uint16_t* v, float* out,
+                                 void* stream);
+dz_status dz_gqa_prefill_at(dz_ctx* ctx, int layer, int seq, int64_t start_pos, int64_t T, const float* q_gate,
+                            const float* k, const float* v, float* out, void* stream);
 /* Chunked (C=64) Gated DeltaNet prefill equal to the token-recurrent reference
  * (model/forward.rs:897-1059).  qkv [T][10240], alpha/beta [T][48], z [T][6144],
  * y [T][v_head_count*128]. */
@@ -168,10 +183,12 @@ dz_status dz_gdn_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_i
  * updates as dz_gqa_decode; its split-K scratch lives in one fixed device array
  * inside the library (about 13.6 MiB per GPU that loads the library, held until
  * exit).  Limits: at most 64 sequences per call (DZ_EINVAL beyond that); the
- * split-K chunk grows so that a call needs at most 2048 work items.  All calls
- * on a device share the array: calls that overlap on the GPU race, so order
- * them.  The first call on each device looks up the array's device address;
- * make that first call before any stream capture begins.
+ * split-K chunk is dz_gqa_decode's, doubled until a call needs at most 2048 work
+ * items -- identical results when no doubling is needed, equal to f32 rounding
+ * otherwise.  All calls on a device share the array: calls that overlap on the
+ * GPU race, so order them.  The first call on each device looks up the array's
+ * device address (again after the device's context changes); make that first
+ * call before any stream capture begins.
  * No counterpart in the reference (the reference runs on the CPU and never
  * allocates device memory). */
 dz_status dz_gqa_decode_noalloc(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* q_gate,

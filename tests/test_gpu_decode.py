@@ -222,3 +222,33 @@ def test_error_paths(dz):
     assert e.value.status == 6
     assert ctx.kv_len(1, 0) == 2
     ctx.close()
+
+
+def test_gqa_decode_explicit_positions(dz):
+    """dz_gqa_decode_at: the RoPE position comes from the caller (ModelState::pos,
+    model/forward.rs:230-238) while the KV slot stays the cache length."""
+    seed = O.SEED0 + 4321
+    lens = [300, 41]
+    ctx, (qn, kn), _ = make_ctx(dz, [n + 4 for n in lens] + [600], seed=seed)
+    kvs = []
+    for s, n in enumerate(lens):
+        kf, vf = O.normal(seed + 10 + s, (n, 4, 256)), O.normal(seed + 20 + s, (n, 4, 256))
+        ctx.kv_import(1, s, kf, vf)
+        kvs.append(O.OracleKv.from_raw(kf, vf, cap=n + 4))
+    pos = [300 + 237, 7]                  # ahead of and behind the slot
+    qg, k, v = O.normal(seed + 1, (2, 12288)), O.normal(seed + 2, (2, 1024)), O.normal(seed + 3, (2, 1024))
+    out = torch.empty(2, 6144, device="cuda")
+    ctx.gqa_decode(1, [0, 1], _dev(qg), _dev(k), _dev(v), out, pos=pos)
+    got = out.cpu().numpy()
+    for s in range(2):
+        want = O.gqa_decode(qg[s], k[s], v[s], qn, kn, kvs[s], pos=pos[s])
+        assert_close(got[s], want, TOL_F32, f"seq {s} at pos {pos[s]}")
+        ke, _ = ctx.kv_export(1, s)
+        assert ke.shape[0] == lens[s] + 1
+        assert_close(ke[lens[s]], kvs[s].k[:, lens[s]], 1e-5, "appended K rotated at pos")
+    # out-of-table positions are rejected before anything runs
+    from daiza_b200 import _ffi
+    with pytest.raises(_ffi.DzError):
+        ctx.gqa_decode(1, [0], _dev(qg[:1]), _dev(k[:1]), _dev(v[:1]), out[:1], pos=[600])
+    assert ctx.kv_len(1, 0) == lens[0] + 1
+    ctx.close()

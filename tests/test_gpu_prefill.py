@@ -138,3 +138,29 @@ def test_gqa_prefill_full_8192_sampled_rows():
     assert np.all(np.isfinite(out.cpu().numpy()))
     assert ctx.device_error() == 0
     ctx.close()
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_gqa_prefill_explicit_start_pos(dtype):
+    """dz_gqa_prefill(_bf16)_at: token t is rotated at start_pos + t
+    (model/forward.rs:550-557) while its KV slot is len + t."""
+    seed = O.SEED0 + 3900
+    T, n_prior, start = 150, 40, 1000
+    ctx, qn, kn = make_ctx([n_prior + T + 4, start + T + 8], seed)
+    qg, k, v = O.normal(seed + 1, (T, 12288)), O.normal(seed + 2, (T, 1024)), O.normal(seed + 3, (T, 1024))
+    if dtype == "bf16":
+        qg, k, v = _bf16_round(qg), _bf16_round(k), _bf16_round(v)
+    kf, vf = O.normal(seed + 4, (n_prior, 4, 256)), O.normal(seed + 5, (n_prior, 4, 256))
+    ctx.kv_import(1, 0, kf, vf)
+    kv = O.OracleKv.from_raw(kf, vf, cap=n_prior + T + 4)
+    want = O.gqa_prefill(qg, k, v, qn, kn, kv, start_pos=start, n_threads=8)
+    tdt = torch.bfloat16 if dtype == "bf16" else None
+    out = torch.empty(T, 6144, device="cuda")
+    ctx.gqa_prefill(1, 0, _dev(qg, tdt), _dev(k, tdt), _dev(v, tdt), out, start_pos=start)
+    # f32 inputs are converted on device: the products run in bf16 either way
+    assert_close(out.cpu().numpy(), want, TOL_BF16, f"prefill at start_pos ({dtype})")
+    ke, ve = ctx.kv_export(1, 0)
+    assert ke.shape[0] == n_prior + T
+    assert np.array_equal(ve, kv.v[:, :n_prior + T].transpose(1, 0, 2))
+    assert_close(ke, kv.k[:, :n_prior + T].transpose(1, 0, 2), TOL_F32, "K cache rotated at start_pos + t")
+    ctx.close()

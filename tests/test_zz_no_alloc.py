@@ -97,3 +97,67 @@ def test_noalloc_rejects_batches_beyond_its_limit():
     assert "64" in lib.dz_last_error(ctx.h).decode()
     assert ctx.kv_len(1, 0) == 0
     ctx.close()
+
+
+def _decode_chunk(n_sm, kvc, lens):
+    """The split-K chunk dz_gqa_decode picks for a batch (the library's decode_chunk)."""
+    total, nmax = int(sum(n + 1 for n in lens)), int(max(n + 1 for n in lens))
+    chunk = (total * kvc) // (n_sm * 16)
+    chunk = min(max(chunk, 16), 1024)
+    chunk = max(chunk, -(-nmax // 128))
+    return -(-chunk // 16) * 16
+
+
+def test_noalloc_doubled_chunk_matches():
+    """64 sequences of about 8200 cached positions: dz_gqa_decode's split would need
+    more than the 2048 work items the fixed scratch holds, so the no-allocation entry
+    point doubles the chunk (past 1024 positions).  Its output must match the regular
+    entry point's, and one sequence is also checked against the oracle."""
+    import daiza_b200 as dz
+    from daiza_b200 import _ffi
+
+    seed = O.SEED0 + 5250
+    rng = np.random.default_rng(seed)
+    lens = [int(x) for x in rng.integers(8150, 8250, size=64)]
+    n_sm = torch.cuda.get_device_properties(0).multi_processor_count
+    chunk = _decode_chunk(n_sm, 4, lens)
+    items = lambda c: 4 * sum(-(-(n + 1) // c) for n in lens)   # noqa: E731
+    assert items(chunk) > 2048, "case must exercise the chunk doubling"
+    while items(chunk) > 2048:
+        chunk *= 2
+    assert chunk > 1024 and items(chunk) <= 2048
+    cfg = dz.default_config(n_layers=2, full_attention_interval=2)
+    ctx = dz.Context(0, cfg)
+    qn, kn = O.attn_params(seed)
+    ctx.set_attn_params(1, qn, kn)
+    ctx.set_ssm_params(0, *O.ssm_params(seed + 1))
+    ctx.cache_create([n + 2 for n in lens] * 2)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    for i, n in enumerate(lens):
+        kf = torch.randn(n, 4, 256, device="cuda", generator=gen)
+        vf = torch.randn(n, 4, 256, device="cuda", generator=gen)
+        ctx.kv_import(1, i, kf, vf)
+        ctx.kv_import(1, i + 64, kf, vf)
+    kf0, vf0 = ctx.kv_export(1, 0)
+    kv0 = O.OracleKv.from_raw(kf0, vf0, cap=lens[0] + 2)
+    B = 64
+    qg = _dev(O.normal(seed + 2, (B, 12288)))
+    k = _dev(O.normal(seed + 3, (B, 1024)))
+    v = _dev(O.normal(seed + 4, (B, 1024)))
+    out_a = torch.empty(B, 6144, device="cuda")
+    out_b = torch.empty(B, 6144, device="cuda")
+    ctx.gqa_decode(1, np.arange(B, dtype=np.int32), qg, k, v, out_a)
+    ids_b = np.arange(B, 2 * B, dtype=np.int32)
+    lib = _ffi.lib()
+    st = lib.dz_gqa_decode_noalloc(ctx.h, 1, B, ids_b.ctypes.data_as(C.c_void_p), C.c_void_p(qg.data_ptr()),
+                                   C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), C.c_void_p(out_b.data_ptr()),
+                                   C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == _ffi.DZ_OK, lib.dz_last_error(ctx.h).decode()
+    a, b = out_a.cpu().numpy(), out_b.cpu().numpy()
+    assert np.all(np.isfinite(b))
+    assert rel_err(b, a) <= TOL_F32
+    want0 = O.gqa_decode(qg[0].cpu().numpy(), k[0].cpu().numpy(), v[0].cpu().numpy(), qn, kn, kv0)
+    assert rel_err(b[0], want0) <= TOL_F32
+    assert ctx.device_error() == 0
+    ctx.close()
