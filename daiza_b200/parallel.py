@@ -17,10 +17,37 @@ Two modes, as the north star partitions the work:
   the causal work is balanced); v heads are always 48 / world per rank.
 
 Nothing here moves data between GPUs except `torch.distributed.all_gather_into_tensor`.
+
+Failure handling: the process group is created with a short, explicit timeout
+(`PG_TIMEOUT_S`, overridable by DZ_PG_TIMEOUT_S), so a rank that leaves or never
+joins makes its peers' next collective end with an error instead of hanging;
+`all_gather_rows` reports any collective failure as DzError(DZ_ENCCL).
 """
+import datetime
+import os
 from dataclasses import dataclass
 
 import numpy as np
+
+from ._ffi import DZ_ENCCL, DzError
+
+PG_TIMEOUT_S = 60.0
+
+
+def pg_timeout():
+    """Timeout of the process group's collectives (DZ_PG_TIMEOUT_S, default 60 s)."""
+    return datetime.timedelta(seconds=float(os.environ.get("DZ_PG_TIMEOUT_S", PG_TIMEOUT_S)))
+
+
+def init_process_group(backend="nccl", device=None, rank=None, world=None):
+    """torch.distributed.init_process_group with the library's short timeout."""
+    import torch.distributed as dist
+    kw = {"timeout": pg_timeout()}
+    if device is not None and backend == "nccl":
+        kw["device_id"] = device
+    if rank is not None:
+        kw["rank"], kw["world_size"] = rank, world
+    dist.init_process_group(backend, **kw)
 
 HKV, GRP, HD, SSM_HV, SSM_D = 4, 6, 256, 48, 128
 
@@ -89,21 +116,27 @@ def assemble_gdn(gathered, plans):
     return torch.cat(list(gathered), dim=1)
 
 
-def all_gather_rows(local, group=None):
-    """All-gather equal-shaped per-rank tensors -> list (NCCL: one
-    all_gather_into_tensor; gloo: all_gather)."""
+def all_gather_rows(local, group=None, out=None):
+    """All-gather equal-shaped per-rank tensors -> list of per-rank views (NCCL:
+    one all_gather_into_tensor into `out` [world, *local.shape] when given, so a
+    caller can keep one buffer per shape; gloo: all_gather).  A failed collective
+    (a peer left, the process-group timeout ran out) raises DzError(DZ_ENCCL)."""
     import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
     if world == 1:
         return [local]
-    if dist.get_backend(group) == "nccl":
-        out = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
-        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
-        return list(out.unbind(0))
-    parts = [torch.empty_like(local) for _ in range(world)]
-    dist.all_gather(parts, local.contiguous(), group=group)
-    return parts
+    try:
+        if dist.get_backend(group) == "nccl":
+            if out is None:
+                out = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+            dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+            return list(out.unbind(0))
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local.contiguous(), group=group)
+        return parts
+    except RuntimeError as e:             # torch's DistBackendError / DistError derive from it
+        raise DzError(DZ_ENCCL, f"all-gather of head outputs failed: {e}") from e
 
 
 def assemble_gqa_prefill(gathered, plans):
@@ -136,13 +169,26 @@ class ShardedStack:
                                     qtile_split=(self.plan.pair_index, self.plan.pair_count))
         self.ctx = engine.Context(device, cfg)
         self.n_layers = n_layers
+        self.attn = [self.ctx.is_attention(layer) for layer in range(n_layers)]
         for layer in range(n_layers):
-            if self.ctx.is_attention(layer):
+            if self.attn[layer]:
                 self.ctx.set_attn_params(layer, *params(layer, "attn"))
             else:
                 self.ctx.set_ssm_params(layer, *params(layer, "ssm"))
         self.ctx.cache_create(kv_caps)
         self.n_seqs = n_seqs
+        self._bufs = {}
+
+    def _gather(self, t):
+        """all_gather_rows into a buffer kept per (shape, dtype)."""
+        import torch
+        if self.world == 1:
+            return [t]
+        key = (tuple(t.shape), t.dtype)
+        buf = self._bufs.get(key)
+        if buf is None:
+            buf = self._bufs[key] = torch.empty((self.world,) + key[0], dtype=t.dtype, device=t.device)
+        return all_gather_rows(t, self.group, out=buf)
 
     # inputs: dict with full-width tensors; slices are taken once by the caller
     def slice_inputs(self, q_gate, k, v):
@@ -165,14 +211,15 @@ class ShardedStack:
         out = torch.empty(len(rows), self.plan.n_q_heads * HD, device=qg.device)
         vc = self.plan.v_heads[1] - self.plan.v_heads[0]
         y = torch.empty(self.n_seqs, vc * SSM_D, device=qg.device)
+        all_rows = np.arange(self.n_seqs, dtype=np.int32)
         last = {}
         for layer in range(self.n_layers):
-            if self.ctx.is_attention(layer):
+            if self.attn[layer]:
                 self.ctx.gqa_decode(layer, rows, qg, ks, vs, out)
-                last["gqa"] = all_gather_rows(out, self.group)
+                last["gqa"] = self._gather(out)
             else:
-                self.ctx.gdn_decode(layer, list(range(self.n_seqs)), *gdn_in, y)
-                last["gdn"] = all_gather_rows(y, self.group)
+                self.ctx.gdn_decode(layer, all_rows, *gdn_in, y)
+                last["gdn"] = self._gather(y)
         return (assemble_gqa(last["gqa"], self.plans, self.n_seqs) if "gqa" in last else None,
                 assemble_gdn(last["gdn"], self.plans) if "gdn" in last else None)
 
@@ -187,12 +234,12 @@ class ShardedStack:
         y = torch.empty(T, vc * SSM_D, device=qg.device)
         last = {}
         for layer in range(self.n_layers):
-            if self.ctx.is_attention(layer):
+            if self.attn[layer]:
                 self.ctx.gqa_prefill(layer, seq, qg, ks, vs, out)
-                last["gqa"] = all_gather_rows(out, self.group)
+                last["gqa"] = self._gather(out)
             else:
                 self.ctx.gdn_prefill(layer, seq, *gdn_in, y)
-                last["gdn"] = all_gather_rows(y, self.group)
+                last["gdn"] = self._gather(y)
         return (assemble_gqa_prefill(last["gqa"], self.plans) if "gqa" in last else None,
                 assemble_gdn(last["gdn"], self.plans) if "gdn" in last else None)
 
