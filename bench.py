@@ -1,16 +1,25 @@
-"""Benchmark of the hybrid-attention hot path (BASELINE.json config 2).
+"""Benchmark of the hybrid-attention hot path (BASELINE.json configs 0-4).
 
-Workload ("step"): batched hybrid decode -- 64 sequences per GPU, each with a
-ragged KV cache of L_i ~ U{512..32768} cached positions (seeded), advance one
-token through one gated GQA layer (dz_gqa_decode) and one Gated DeltaNet layer
-(dz_gdn_decode).  Inputs are synthetic N(0,1) activations (projections are out
-of scope), KV contents N(0,1), DeltaNet state N(0, 0.02).  Sequence-sharded
-across GPUs with no collective: every rank owns its own 64 sequences (weak
-scaling).  The per-step KV + state traffic (~9 GB) is far above the 126 MB L2,
-so no flush is needed between steps.
+Headline ("step", the JSON line's value): BASELINE config 2, batched hybrid
+decode -- 64 sequences in total with ragged KV caches of L_i ~ U{512..32768}
+cached positions (seeded), each advancing one token through one gated GQA layer
+(dz_gqa_decode) and one Gated DeltaNet layer (dz_gdn_decode).  Sequence-sharded
+across the GPUs with no collective: the 64 sequences are split by LPT on
+L_i + 1 (strong scaling).  Inputs are synthetic N(0,1) activations (projections
+are out of scope), KV contents N(0,1), DeltaNet state N(0, 0.02).  Per-step
+KV + state traffic (~9 GB in total) is far above the 126 MB L2, so no flush is
+needed between steps.
 
-Metric: decode tokens/s (whole job), with the achieved HBM GB/s of the
-dominant kernel group against the measured copy bandwidth.
+Extra keys on the same line:
+  config0 / config1  single-layer decode (config 0: one GQA layer at position
+                     2048; config 1: one Gated DeltaNet layer), many back-to-back
+                     layer instances over buffers larger than L2, replayed from a
+                     CUDA graph; N = 1 only
+  prefill            config 3 (T = 8192): GQA prefill TFLOP/s against the bf16
+                     peak, Gated DeltaNet prefill time, CPU baselines; N = 1 only
+  stack              config 4: the 64-layer stack head-sharded over the ranks
+                     with an NCCL all-gather per layer (decode B = 8 at context
+                     131072, prefill T = 32768); every N
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -27,17 +36,25 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "hybrid-attn decode tok/s + % HBM BW; prefill attn TFLOP/s vs peak"
-B_PER_RANK = 64
+N_SEQ = 64
 LEN_LO, LEN_HI = 512, 32768
 SEED0 = 0xDA12A000 + 2      # config 2
 
 HQ, HKV, GRP, HD = 24, 4, 6, 256
 SSM_HV, SSM_D, QKV_LEN, INNER = 48, 128, 10240, 6144
 
+# DRAM bytes that ncu counted for the split-K attention kernel divided by its
+# algorithmic K/V bytes, on the capture summarised in
+# profiles/gqa_split_kernel_config2.md; the roofline's `traffic` is this ratio
+# times the algorithmic bytes of the timed launch (traffic grows with the KV
+# positions read).  None until measured.
+GQA_SPLIT_TRAFFIC_RATIO = None
 
-def seq_lengths(rank):
-    rng = np.random.default_rng(SEED0 + 7919 * rank)
-    return rng.integers(LEN_LO, LEN_HI + 1, size=B_PER_RANK).astype(np.int64)
+
+def seq_lengths():
+    """The 64 config-2 cache lengths (seeded, identical on every rank)."""
+    rng = np.random.default_rng(SEED0)
+    return rng.integers(LEN_LO, LEN_HI + 1, size=N_SEQ).astype(np.int64)
 
 
 def layer_params(seed):
@@ -63,7 +80,7 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-# algorithmic bytes (SURVEY 8d formulas, counted per step)
+# algorithmic bytes per step (K/V rows read once, inputs read once, outputs written once)
 def gqa_bytes(lens_before):
     n = np.asarray(lens_before, np.int64) + 1
     kv_read = int(n.sum()) * HKV * HD * 4 * 2
@@ -77,6 +94,16 @@ def gdn_bytes(B):
                + QKV_LEN * 4 + 2 * SSM_HV * 4           # qkv, alpha, beta
                + INNER * 4 * 2)                         # z in, y out
     return B * per_seq + 4 * QKV_LEN * 4 + (2 * SSM_HV + SSM_D) * 4   # + conv weights and params once
+
+
+def gqa_prefill_flops(T, base=0):
+    """QK^T and PV over the causal range: 4 * 24 * 256 * sum_t (base + t + 1)."""
+    return 4.0 * HQ * HD * (T * base + T * (T + 1) / 2)
+
+
+def gdn_prefill_flops(T, heads=SSM_HV, C=64):
+    """Chunked form per (chunk, head): 10 C^2 d + 6 C d^2 + (2/3) C^3."""
+    return (T // C) * heads * (10 * C * C * SSM_D + 6 * C * SSM_D * SSM_D + (2 / 3) * C ** 3)
 
 
 class Clocks:
@@ -153,29 +180,35 @@ class Clocks:
 
 
 # ---------------------------------------------------------------------------
-# reference arm / CPU baseline: the oracle (C++ restatement of the AVX2 path)
+# reference arm / CPU baselines: the oracle (C++ restatement of the AVX2 path)
 # ---------------------------------------------------------------------------
 class CpuWorkload:
-    """A bounded sample of config 2 for the oracle (C++ restatement of the
-    reference's AVX2 path): n_seq of the 64 sequences (evenly spaced, their real
-    lengths), built once; step() advances every sampled sequence by one token
-    through both layers."""
+    """Config 2 for the oracle: the sequences `pick` (indices into the 64), their
+    real lengths, built once; step() advances every one of them by one token
+    through both layers.  KV rows are tiled from one seeded random block of 4096
+    positions (the attention's cost does not depend on the values)."""
 
-    def __init__(self, n_seq, max_steps, rank=0):
+    def __init__(self, pick, max_steps):
         import oracle as O
         self.O = O
-        lens = seq_lengths(rank)
-        self.pick = lens[:: max(1, B_PER_RANK // n_seq)][:n_seq]
+        lens = seq_lengths()
+        self.pick = np.asarray(pick)
+        self.lens = lens[self.pick]
         (self.qn, self.kn), self.p = layer_params(SEED0)
+        blk_k = O.normal(SEED0 + 500, (HKV, 4096, HD))
+        blk_v = O.normal(SEED0 + 600, (HKV, 4096, HD))
+        st0 = O.normal(SEED0 + 700, (SSM_HV, SSM_D, SSM_D), 0.0, 0.02)
+        h0 = O.normal(SEED0 + 800, (4, QKV_LEN))
         self.kvs, self.sts = [], []
-        for i, n in enumerate(self.pick):
-            kv = O.OracleKv(int(n) + max_steps)
-            kv.k[:, :n] = O.normal(SEED0 + 500 + i, (HKV, int(n), HD))
-            kv.v[:, :n] = O.normal(SEED0 + 600 + i, (HKV, int(n), HD))
-            kv.len = int(n)
+        for n in self.lens:
+            n = int(n)
+            kv = O.OracleKv(n + max_steps)
+            reps = -(-n // 4096)
+            kv.k[:, :n] = np.tile(blk_k, (1, reps, 1))[:, :n]
+            kv.v[:, :n] = np.tile(blk_v, (1, reps, 1))[:, :n]
+            kv.len = n
             self.kvs.append(kv)
-            self.sts.append(O.OracleSsm(O.normal(SEED0 + 700 + i, (SSM_HV, SSM_D, SSM_D), 0.0, 0.02),
-                                        O.normal(SEED0 + 800 + i, (4, QKV_LEN)), 0))
+            self.sts.append(O.OracleSsm(st0, h0, 0))
         Bs = len(self.pick)
         self.qg = O.normal(SEED0 + 1, (Bs, HQ * 2 * HD))
         self.k = O.normal(SEED0 + 2, (Bs, HKV * HD))
@@ -192,32 +225,61 @@ class CpuWorkload:
         return time.perf_counter() - t0
 
 
-def cpu_baseline(n_seq_sample=8, steps=1, n_threads=1, rank=0):
-    w = CpuWorkload(n_seq_sample, steps, rank)
-    dt = sum(w.step(n_threads) for _ in range(steps))
-    return len(w.pick) * steps / dt, dt, w.pick
+def cpu_baseline_decode(steps=1):
+    """Config 2, 8 of the 64 sequences, one thread (the reference decodes one
+    sequence at a time, attention and scan single-threaded)."""
+    pick = np.arange(0, N_SEQ, N_SEQ // 8)
+    w = CpuWorkload(pick, steps)
+    dt = sum(w.step(1) for _ in range(steps))
+    return {"value": len(pick) * steps / dt, "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": f"8 of the 64 sequences (lengths {list(map(int, w.lens))}), {steps} decode step(s) of both "
+                      f"layers, single thread like the reference's decode attention/scan; {dt:.2f} s"}
+
+
+def cpu_baseline_prefill(T=1024):
+    """Config 3 on the host cores: the oracle's parallel prefills (GQA over
+    (token, kv head) units, Gated DeltaNet over v heads, as the reference's
+    forward.rs:643,920,1025) at T tokens, all cores."""
+    import oracle as O
+    cores = os.cpu_count() or 1
+    (qn, kn), p = layer_params(SEED0 + 3)
+    qg, k, v = O.normal(SEED0 + 31, (T, HQ * 2 * HD)), O.normal(SEED0 + 32, (T, HKV * HD)), \
+        O.normal(SEED0 + 33, (T, HKV * HD))
+    t0 = time.perf_counter()
+    O.gqa_prefill(qg, k, v, qn, kn, O.OracleKv(T), n_threads=cores)
+    tg = time.perf_counter() - t0
+    qkv, a, b, z = O.normal(SEED0 + 34, (T, QKV_LEN)), O.normal(SEED0 + 35, (T, SSM_HV)), \
+        O.normal(SEED0 + 36, (T, SSM_HV)), O.normal(SEED0 + 37, (T, INNER))
+    t0 = time.perf_counter()
+    O.gdn_prefill(qkv, a, b, z, p, O.OracleSsm(), n_threads=cores)
+    td = time.perf_counter() - t0
+    return {"gqa": {"value": gqa_prefill_flops(T) / tg / 1e12, "unit": "TFLOP/s", "ms": tg * 1e3, "cores": cores,
+                    "kind": "port", "sample": f"T={T} tokens (config 3 has 8192; work grows as T^2)"},
+            "gdn": {"value": T / td, "unit": "tok/s", "ms": td * 1e3, "cores": cores, "kind": "port",
+                    "sample": f"T={T} tokens, token-recurrent per v head like the reference"}}
 
 
 def run_reference(args):
+    """The reference's CPU path (the oracle port of its AVX2 code) on config 2:
+    all 64 sequences, one decode step of both layers per timed step, one
+    sequence per host thread."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     cores = os.cpu_count() or 1
-    n_seq = min(cores, 32)
-    w = CpuWorkload(n_seq, args.warmup + args.steps, rank)
+    w = CpuWorkload(np.arange(N_SEQ), args.warmup + args.steps)
     for _ in range(args.warmup):
         w.step(cores)
     dts = [w.step(cores) for _ in range(args.steps)]
     wall = sum(dts)
-    value = len(w.pick) * args.steps / wall
-    sample = (f"{len(w.pick)} of the 64 config-2 sequences (evenly spaced, real lengths, "
-              f"{int(np.sum(w.pick))} cached tokens), one decode step of both layers per timed step; "
-              f"one sequence per thread on {cores} host threads (harness parallelisation: the reference "
+    value = N_SEQ * args.steps / wall
+    sample = (f"all {N_SEQ} config-2 sequences ({int(np.sum(w.lens))} cached tokens), one decode step of both layers "
+              f"per timed step; {cores} host threads, one sequence per thread (harness parallelisation: the reference "
               "decodes one sequence at a time)")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * wall / max(1, args.steps),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "config 2: batched hybrid decode, 64 seqs/GPU, "
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "config 2: batched hybrid decode, 64 sequences, "
                                                         "KV U{512..32768}, 1 GQA + 1 GDN layer"},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -228,23 +290,23 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def run_ours(args):
+def _max_over_ranks(dist, dev, x):
+    if dist is None:
+        return x
     import torch
-    import daiza_b200 as dz
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
 
-    lens = seq_lengths(rank)[: args.seqs]
+def bench_config2(dz, torch, dist, dev, local, rank, world, args):
+    """This rank's LPT share of the 64 sequences, timed with CUDA events; the
+    headline value uses the max over ranks."""
+    from daiza_b200 import parallel as P
+    all_lens = seq_lengths()
+    mine = P.lpt_shard(all_lens, world)[rank]
+    lens = all_lens[mine]
+    B = len(lens)
     total_steps = args.warmup + args.steps + args.e2e_steps + 2
     cfg = dz.default_config(n_layers=2, full_attention_interval=2)   # layer 0 GDN, layer 1 GQA
     ctx = dz.Context(local, cfg)
@@ -253,7 +315,7 @@ def run_ours(args):
     ctx.set_ssm_params(0, *sp)
     ctx.cache_create(lens + total_steps)
     g = torch.Generator(device=dev)
-    g.manual_seed(SEED0 + rank)
+    g.manual_seed(SEED0 + 1000 + rank)
     for s, n in enumerate(lens):
         kf = torch.randn(int(n), HKV, HD, device=dev, generator=g)
         vf = torch.randn(int(n), HKV, HD, device=dev, generator=g)
@@ -263,7 +325,6 @@ def run_ours(args):
         hist = torch.randn(4, QKV_LEN, device=dev, generator=g)
         ctx.ssm_import(0, s, st, hist, 0)
     torch.cuda.synchronize()
-    B = len(lens)
     ids = np.arange(B, dtype=np.int32)
     qg = torch.randn(B, HQ * 2 * HD, device=dev, generator=g)
     kk = torch.randn(B, HKV * HD, device=dev, generator=g)
@@ -276,14 +337,9 @@ def run_ours(args):
     y = torch.empty(B, INNER, device=dev)
     stream = torch.cuda.current_stream()
 
-    def step():
-        ctx.gqa_decode(1, ids, qg, kk, vv, out)
-        n1 = ctx.last_launch_count
-        ctx.gdn_decode(0, ids, qkv, al, be, z, y)
-        return n1 + ctx.last_launch_count
-
     for _ in range(args.warmup):
-        step()
+        ctx.gqa_decode(1, ids, qg, kk, vv, out)
+        ctx.gdn_decode(0, ids, qkv, al, be, z, y)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -315,37 +371,24 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = t_start.elapsed_time(t_end)
+    ms_rank = t_start.elapsed_time(t_end)
+    ms = _max_over_ranks(dist, dev, ms_rank)
     gqa_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.steps)]
     gdn_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps)]
-    if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = world * B * args.steps / (ms / 1000.0)
 
-    # bytes per step of the dominant kernel group (GQA decode: prep + split-K + combine)
     gqa_b = np.mean([gqa_bytes(lens_at + i) for i in range(args.steps)])
     gdn_b = gdn_bytes(B)
-    hbm, bf16, peak_kind = peaks()
+    hbm, _, peak_kind = peaks()
     gqa_gbs = gqa_b / (np.mean(gqa_ms) / 1000.0) / 1e9
     gdn_gbs = gdn_b / (np.mean(gdn_ms) / 1000.0) / 1e9
-    step_gbs = (gqa_b + gdn_b) / (ms / args.steps / 1000.0) / 1e9
 
-    # end-to-end through the public C ABI host entry points (pinned host buffers)
+    # end to end through the public C ABI host entry points (pinned host buffers)
     e2e = None
     if args.e2e_steps > 0:
-        hq = torch.empty(B, HQ * 2 * HD, pin_memory=True)
-        hq.copy_(qg.cpu())
-        hk = kk.cpu().pin_memory()
-        hv = vv.cpu().pin_memory()
-        hx = qkv.cpu().pin_memory()
-        ha = al.cpu().pin_memory()
-        hb = be.cpu().pin_memory()
-        hz = z.cpu().pin_memory()
+        host = [t.cpu().pin_memory() for t in (qg, kk, vv, qkv, al, be, z)]
         ho = torch.empty(B, HQ * HD, pin_memory=True)
         hy = torch.empty(B, INNER, pin_memory=True)
-        np_views = [t.numpy() for t in (hq, hk, hv, hx, ha, hb, hz, ho, hy)]
+        nv = [t.numpy() for t in host] + [ho.numpy(), hy.numpy()]
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
@@ -353,68 +396,146 @@ def run_ours(args):
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.e2e_steps):
-            ctx.gqa_decode_host(1, ids, np_views[0], np_views[1], np_views[2], np_views[7])
-            ctx.gdn_decode_host(0, ids, np_views[3], np_views[4], np_views[5], np_views[6], np_views[8])
+            ctx.gqa_decode_host(1, ids, nv[0], nv[1], nv[2], nv[7])
+            ctx.gdn_decode_host(0, ids, nv[3], nv[4], nv[5], nv[6], nv[8])
         e1.record(stream)
         torch.cuda.synchronize()
-        ems = e0.elapsed_time(e1)
-        if dist:
-            t = torch.tensor([ems], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
+        ems = _max_over_ranks(dist, dev, e0.elapsed_time(e1))
         h2d = B * (HQ * 2 * HD + 2 * HKV * HD + QKV_LEN + 2 * SSM_HV + INNER) * 4
         d2h = B * (HQ * HD + INNER) * 4
-        e2e = {"value": world * B * args.e2e_steps / (ems / 1000.0), "unit": "tok/s",
+        e2e = {"value": N_SEQ * args.e2e_steps / (ems / 1000.0), "unit": "tok/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": "dz_gqa_decode_host + dz_gdn_decode_host (pinned host buffers, copies inside the timed region)",
+               "path": "dz_gqa_decode_host + dz_gdn_decode_host (pinned host buffers, copies inside the timed region), "
+                       "max over ranks",
                "steps": args.e2e_steps}
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        v, dt, pick = cpu_baseline(n_seq_sample=8, steps=args.cpu_steps, n_threads=1)
-        cpu = {"value": v, "unit": "tok/s", "cores": 1, "kind": "port",
-               "sample": f"8 of the 64 sequences (lengths {list(map(int, pick))}), {args.cpu_steps} decode step(s) "
-                         f"of both layers, single thread like the reference's decode attention/scan; {dt:.2f} s"}
-
-    prefill = None
-    if not args.no_prefill:
-        prefill = run_prefill(dz, torch, local, args)
-
     err = ctx.device_error()
-    if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": "config 2: batched hybrid decode, 64 seqs/GPU, KV lengths U{512..32768} "
-                                       "(seeded), 1 gated GQA + 1 Gated DeltaNet layer, f32 caches",
-                           "seqs_per_gpu": B, "kv_tokens_per_gpu": int(lens_at.sum()),
-                           "parallelism": f"sequence-sharded x{world}, no collective",
-                           "l2": "no flush: per-step KV+state traffic ~9 GB >> 126 MB L2"},
-                "hbm_gbs_step": step_gbs, "hbm_frac_step": step_gbs / hbm,
-                "roofline": {"bound": "hbm", "kernel": "dz_gqa_decode (prep + split-K + combine)",
-                             "achieved": gqa_gbs, "peak": hbm, "unit": "GB/s", "frac": gqa_gbs / hbm,
-                             "traffic": None, "peak_kind": f"{peak_kind} hbm_gbs",
-                             "bytes_per_launch": gqa_b, "ms_per_launch": float(np.mean(gqa_ms))},
-                "gdn": {"achieved_gbs": gdn_gbs, "frac": gdn_gbs / hbm, "bytes": gdn_b,
-                        "ms": float(np.mean(gdn_ms))},
-                "gpu_launches": launches, "clocks": clk, "e2e": e2e, "cpu_baseline": cpu, "prefill": prefill,
-                "device_error": err}
-        if clk is None and clocks.raw:
-            line["clocks_raw_head"] = clocks.raw[:300]
-        print(json.dumps(line))
     ctx.close()
-    if dist:
-        dist.destroy_process_group()
-    return 0
+    traffic = None if GQA_SPLIT_TRAFFIC_RATIO is None else GQA_SPLIT_TRAFFIC_RATIO * gqa_b
+    return {"ms": ms, "ms_rank": ms_rank, "B": B, "kv_tokens": int(lens_at.sum()), "clk": clk, "clocks": clocks,
+            "launches": launches, "e2e": e2e, "device_error": err,
+            "roofline": {"bound": "hbm", "kernel": "dz_gqa_decode (prep + split-K + combine)", "achieved": gqa_gbs,
+                         "peak": hbm, "unit": "GB/s", "frac": gqa_gbs / hbm, "traffic": traffic,
+                         "peak_kind": f"{peak_kind} hbm_gbs", "bytes_per_launch": gqa_b,
+                         "ms_per_launch": float(np.mean(gqa_ms)), "rank": rank},
+            "gdn": {"achieved_gbs": gdn_gbs, "frac": gdn_gbs / hbm, "bytes": gdn_b, "ms": float(np.mean(gdn_ms))},
+            "step_gbs": (gqa_b + gdn_b) / (ms_rank / args.steps / 1000.0) / 1e9}
+
+
+def bench_single_layer(dz, torch, dev, local, kind, reps=20):
+    """Configs 0 and 1: one decode step of one layer, measured over many
+    back-to-back layer instances (16 GQA layers x 16.8 MB of KV, or 96 Gated
+    DeltaNet layers x 3.1 MB of state: 269 MB and 302 MB, both above the 126 MB
+    L2, so every instance reads its bytes from HBM), captured once into a CUDA graph and
+    replayed (every replay rewrites the same cache slot / conv slot, which is
+    the same work as a fresh step)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED0 + 7 + (kind == "gdn"))
+    if kind == "gqa":
+        M, n_prior = 16, 2048
+        cfg = dz.default_config(n_layers=4 * M, full_attention_interval=4)
+        layers = [4 * i + 3 for i in range(M)]
+    else:
+        M = 96
+        cfg = dz.default_config(n_layers=M, full_attention_interval=M + 1)
+        layers = list(range(M))
+    ctx = dz.Context(local, cfg)
+    for layer in range(cfg.n_layers):
+        a, s_ = layer_params(SEED0 + 100 + layer)
+        if ctx.is_attention(layer):
+            ctx.set_attn_params(layer, *a)
+        else:
+            ctx.set_ssm_params(layer, *s_)
+    if kind == "gqa":
+        ctx.cache_create([n_prior + 2])
+        for layer in layers:
+            kf = torch.randn(n_prior, HKV, HD, device=dev, generator=g)
+            vf = torch.randn(n_prior, HKV, HD, device=dev, generator=g)
+            ctx.kv_import(layer, 0, kf, vf)
+        qg = torch.randn(1, HQ * 2 * HD, device=dev, generator=g)
+        kk = torch.randn(1, HKV * HD, device=dev, generator=g)
+        vv = torch.randn(1, HKV * HD, device=dev, generator=g)
+        out = torch.empty(1, HQ * HD, device=dev)
+
+        def one_round():
+            for layer in layers:
+                ctx.gqa_decode(layer, [0], qg, kk, vv, out)
+
+        def rewind():
+            for layer in layers:
+                ctx.kv_truncate(layer, 0, n_prior)
+        bytes_per = gqa_bytes([n_prior])
+    else:
+        ctx.cache_create([4])
+        for layer in layers:
+            st = torch.randn(SSM_HV, SSM_D, SSM_D, device=dev, generator=g) * 0.02
+            hist = torch.randn(4, QKV_LEN, device=dev, generator=g)
+            ctx.ssm_import(layer, 0, st, hist, 0)
+        qkv = torch.randn(1, QKV_LEN, device=dev, generator=g)
+        al = torch.randn(1, SSM_HV, device=dev, generator=g)
+        be = torch.randn(1, SSM_HV, device=dev, generator=g)
+        z = torch.randn(1, INNER, device=dev, generator=g)
+        y = torch.empty(1, INNER, device=dev)
+
+        def one_round():
+            for layer in layers:
+                ctx.gdn_decode(layer, [0], qkv, al, be, z, y)
+
+        def rewind():
+            pass
+        bytes_per = gdn_bytes(1)
+    for _ in range(2):
+        one_round()
+        rewind()
+    torch.cuda.synchronize()
+    graph = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            one_round()
+        rewind()
+    except Exception as e:  # noqa: BLE001 -- fall back to eager issue and say so
+        graph = None
+        note = f"eager (graph capture failed: {type(e).__name__})"
+        torch.cuda.synchronize()
+        rewind()
+    else:
+        note = "CUDA graph of one round, replayed"
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        graph.replay() if graph is not None else one_round()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        if graph is not None:
+            graph.replay()
+        else:
+            one_round()
+            rewind()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    err = ctx.device_error()
+    del graph
+    ctx.close()
+    us = ms * 1000.0 / (reps * len(layers))
+    hbm, _, kind_p = peaks()
+    gbs = bytes_per / (us * 1e-6) / 1e9
+    return {"workload": ("config 0: one gated GQA decode step at position 2048 (2048 cached positions), 24/4 heads, "
+                         "D=256" if kind == "gqa" else
+                         "config 1: one Gated DeltaNet decode step, 16/48 heads, d=128, state N(0,0.02)"),
+            "us_per_layer_step": us, "tok_s": 1e6 / us, "bytes": bytes_per, "achieved_gbs": gbs, "peak_gbs": hbm,
+            "frac": gbs / hbm, "peak_kind": f"{kind_p} hbm_gbs", "instances": len(layers), "replays": reps,
+            "issue": note, "device_error": err}
 
 
 PF_T = 8192
 
 
-def run_prefill(dz, torch, local, args):
-    """Config 3 GQA prefill: one sequence, T=8192 bf16 tokens, positions 0..8191,
-    through dz_gqa_prefill_bf16 (prep + tcgen05 attention).  FLOPs counted as
-    4 * 24 * 256 * sum_{t<T}(t+1) (QK^T and PV over the causal range)."""
+def bench_prefill(dz, torch, local, args):
+    """Config 3: one sequence, T=8192 tokens, positions 0..8191.  GQA prefill with
+    bf16 q/k/v (prep + tcgen05 attention); Gated DeltaNet prefill with f32
+    qkv/alpha/beta/z from a zero state (prep + ring + intra + chain)."""
     dev = torch.device("cuda", local)
     cfg = dz.default_config(n_layers=2, full_attention_interval=2)
     ctx = dz.Context(local, cfg)
@@ -445,7 +566,6 @@ def run_prefill(dz, torch, local, args):
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1))
     launches = ctx.last_launch_count
-    # Gated DeltaNet prefill, same T: f32 qkv/alpha/beta/z, zero state and history
     qkv = torch.randn(PF_T, QKV_LEN, device=dev, generator=g)
     al = torch.randn(PF_T, SSM_HV, device=dev, generator=g)
     be = torch.randn(PF_T, SSM_HV, device=dev, generator=g)
@@ -465,49 +585,38 @@ def run_prefill(dz, torch, local, args):
         if it >= 3:
             gtimes.append(e0.elapsed_time(e1))
     glaunches = ctx.last_launch_count
+    err = ctx.device_error()
     ctx.close()
     gms = float(np.median(gtimes))
-    C, d = 64, SSM_D
-    g_flops = (PF_T // C) * SSM_HV * (10 * C * C * d + 6 * C * d * d + (2 / 3) * C ** 3)
+    g_flops = gdn_prefill_flops(PF_T)
     g_bytes = PF_T * (QKV_LEN + 2 * SSM_HV + 2 * INNER) * 4 + SSM_HV * SSM_D * SSM_D * 4 * 2
-    hbm, _, _ = peaks()
-    gdn = {"workload": "config 3 Gated DeltaNet prefill, T=8192, f32, chunk 64, zero state",
-           "ms": gms, "algorithmic_gflop": g_flops / 1e9, "tflops": g_flops / (gms / 1000.0) / 1e12,
-           "bytes": g_bytes, "gbs": g_bytes / (gms / 1000.0) / 1e9, "hbm_frac": g_bytes / (gms / 1000.0) / 1e9 / hbm,
-           "launches_per_call": glaunches,
-           "note": "f32 CUDA-core WY/UT chunk kernels (intra-chunk parallel, inter-chunk sequential per head)"}
-    flops = 4.0 * HQ * HD * (PF_T * (PF_T + 1) / 2)
+    hbm, bf16, kind = peaks()
+    gdn = {"workload": "config 3 Gated DeltaNet prefill, T=8192, f32 in/out, chunk 64, zero state",
+           "ms": gms, "tok_s": PF_T / (gms / 1000.0), "algorithmic_gflop": g_flops / 1e9,
+           "tflops": g_flops / (gms / 1000.0) / 1e12, "bytes": g_bytes, "gbs": g_bytes / (gms / 1000.0) / 1e9,
+           "hbm_frac": g_bytes / (gms / 1000.0) / 1e9 / hbm, "launches_per_call": glaunches,
+           "note": "tcgen05 bf16 hi/lo split products (3 per product, f32 accumulate in TMEM): persistent intra-chunk "
+                   "WY kernel + one persistent chain CTA per v head with the state in TMEM"}
+    flops = gqa_prefill_flops(PF_T)
     ms = float(np.median(times))
     tf = flops / (ms / 1000.0) / 1e12
-    _, bf16, kind = peaks()
     return {"workload": "config 3 GQA prefill, T=8192, bf16 q/k/v, 24/4 heads, D=256, causal",
-            "ms": ms, "tflops": tf, "peak_tflops": bf16, "frac": tf / bf16, "peak_kind": f"{kind} bf16_tflops (burst)",
-            "flops": flops, "iters": iters, "launches_per_call": launches,
+            "ms": ms, "tok_s": PF_T / (ms / 1000.0), "tflops": tf, "peak_tflops": bf16, "frac": tf / bf16,
+            "peak_kind": f"{kind} bf16_tflops (burst)", "flops": flops, "iters": iters,
+            "launches_per_call": launches,
             "timed": "dz_gqa_prefill_bf16 = prep (norm/rope/cache append) + tcgen05 attention, median of iters",
-            "gdn": gdn}
+            "gdn": gdn, "device_error": err}
 
 
-def run_stack(args):
+def bench_stack(dz, torch, dist, dev, local, rank, world, args):
     """Config 4: the 64-layer attention stack (48 Gated DeltaNet + 16 GQA layers),
     head-sharded over the ranks with an NCCL all-gather of head outputs after
     every layer.  Decode: batch 8 at context 131072 (KV rows are a synthetic byte
-    pattern).  Prefill: one sequence of 32768 tokens."""
-    import datetime
-    import torch
-    import torch.distributed as dist
+    pattern).  Prefill: one sequence of 32768 tokens.  Times are the max over
+    ranks; strong scaling (the whole problem is split over the ranks)."""
     from daiza_b200 import parallel as P
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if not dist.is_initialized():
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29555")
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
-                                device_id=dev)
     B, CTX, T = 8, args.stack_ctx, args.stack_prefill
-    steps, warm = args.steps, args.warmup
+    steps, warm = args.stack_steps, 2
     plan = P.head_plan(world, rank)
     rows = plan.decode_rows(B)
     caps = [(CTX + steps + warm + 2) if b in rows else 1 for b in range(B)] + [T]
@@ -519,7 +628,7 @@ def run_stack(args):
     stack = P.ShardedStack(local, B, caps, params)
     t0 = time.time()
     for layer in range(64):
-        if stack.ctx.is_attention(layer):
+        if stack.attn[layer]:
             for b in rows:
                 stack.ctx.kv_fill_pattern(layer, b, CTX, 0x3C)
     torch.cuda.synchronize()
@@ -536,24 +645,20 @@ def run_stack(args):
     for _ in range(warm):
         stack.decode_step(gqa_in, gdn)
     torch.cuda.synchronize()
-    dist.barrier()
+    if dist:
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(steps):
         stack.decode_step(gqa_in, gdn)
     e1.record(stream)
     torch.cuda.synchronize()
-    dist.barrier()
-    dms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
-    dist.all_reduce(dms, op=dist.ReduceOp.MAX)
-    dms = float(dms.item())
-    # bytes per decode step on this rank: its KV rows (incl. new token) + its DeltaNet states
+    dms = _max_over_ranks(dist, dev, e0.elapsed_time(e1) / steps)
     ctx_now = CTX + warm + steps // 2
     kvc = plan.kv_heads[1] - plan.kv_heads[0]
     vc = plan.v_heads[1] - plan.v_heads[0]
     rank_bytes = 16 * len(rows) * (ctx_now + 1) * kvc * HD * 4 * 2 + 48 * B * vc * SSM_D * SSM_D * 4 * 2
     hbm, bf16, kind = peaks()
-    # prefill
     pg = torch.randn(T, HQ * 2 * HD, device=dev, generator=g).to(torch.bfloat16)
     pk = torch.randn(T, HKV * HD, device=dev, generator=g).to(torch.bfloat16)
     pv = torch.randn(T, HKV * HD, device=dev, generator=g).to(torch.bfloat16)
@@ -563,7 +668,8 @@ def run_stack(args):
     for it in range(1 + args.stack_prefill_iters):
         stack.ctx.cache_reset(B)
         torch.cuda.synchronize()
-        dist.barrier()
+        if dist:
+            dist.barrier()
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record(stream)
         stack.prefill(B, pin, pgdn)
@@ -571,17 +677,13 @@ def run_stack(args):
         torch.cuda.synchronize()
         if it > 0:
             ptimes.append(a0.elapsed_time(a1))
-    pms = torch.tensor([float(np.median(ptimes))], device=dev)
-    dist.all_reduce(pms, op=dist.ReduceOp.MAX)
-    pms = float(pms.item())
-    gqa_flops = 16 * 4.0 * HQ * HD * (T * (T + 1) / 2)
+    pms = _max_over_ranks(dist, dev, float(np.median(ptimes)))
+    gqa_flops = 16 * gqa_prefill_flops(T)
     err = stack.ctx.device_error()
     stack.close()
-    if rank == 0:
-        print(json.dumps({
-            "metric": METRIC, "workload": "config 4: 64-layer stack (48 GDN + 16 GQA), head-sharded, NCCL all-gather "
-                                          "of head outputs per layer",
-            "n_gpus": world, "scaling": "strong",
+    return {"workload": "config 4: 64-layer stack (48 Gated DeltaNet + 16 gated GQA), head-sharded, NCCL all-gather "
+                        "of head outputs after every layer",
+            "scaling": "strong",
             "decode": {"batch": B, "context": CTX, "ms_per_token_step": dms, "tok_s": B / (dms / 1000.0),
                        "hbm_gbs_per_gpu": rank_bytes / (dms / 1000.0) / 1e9,
                        "hbm_frac_per_gpu": rank_bytes / (dms / 1000.0) / 1e9 / hbm, "steps": steps, "warmup": warm,
@@ -590,36 +692,87 @@ def run_stack(args):
                         "gqa_tflops_whole_job": gqa_flops / (pms / 1000.0) / 1e12,
                         "note": "ms covers all 64 layers incl. per-layer all-gathers (GQA + GDN)"},
             "plan": {"kv_heads_per_rank": kvc, "v_heads_per_rank": vc, "pair_count": plan.pair_count},
-            "kv_fill_s": fill_s, "device_error": err}))
-    dist.destroy_process_group()
+            "kv_fill_s": fill_s, "device_error": err}
+
+
+def run_ours(args):
+    import torch
+    import daiza_b200 as dz
+    from daiza_b200 import parallel as P
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        P.init_process_group("nccl", device=dev)
+
+    c2 = bench_config2(dz, torch, dist, dev, local, rank, world, args)
+    extra = {}
+    if world == 1 and not args.no_single:
+        extra["config0"] = bench_single_layer(dz, torch, dev, local, "gqa")
+        extra["config1"] = bench_single_layer(dz, torch, dev, local, "gdn")
+    if world == 1 and not args.no_prefill:
+        extra["prefill"] = bench_prefill(dz, torch, local, args)
+    if not args.no_stack:
+        torch.cuda.empty_cache()
+        extra["stack"] = bench_stack(dz, torch, dist, dev, local, rank, world, args)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline_decode(steps=args.cpu_steps)
+        if "prefill" in extra:
+            extra["prefill"]["cpu_baseline"] = cpu_baseline_prefill()
+    else:
+        cpu = None
+
+    if rank == 0:
+        ms = c2["ms"]
+        line = {"metric": METRIC, "value": N_SEQ * args.steps / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic",
+                "config": {"workload": "config 2: batched hybrid decode, 64 sequences in total, KV lengths "
+                                       "U{512..32768} (seeded), 1 gated GQA + 1 Gated DeltaNet layer, f32 caches",
+                           "sequences": N_SEQ, "seqs_on_rank0": c2["B"], "kv_tokens_on_rank0": c2["kv_tokens"],
+                           "parallelism": f"sequence-sharded x{world} (LPT on cached length), no collective",
+                           "l2": "no flush: per-step KV+state traffic ~9 GB >> 126 MB L2"},
+                "hbm_gbs_step_rank0": c2["step_gbs"], "roofline": c2["roofline"], "gdn": c2["gdn"],
+                "gpu_launches": c2["launches"], "clocks": c2["clk"], "e2e": c2["e2e"], "cpu_baseline": cpu,
+                "device_error": c2["device_error"]}
+        line.update(extra)
+        if c2["clk"] is None and c2["clocks"].raw:
+            line["clocks_raw_head"] = c2["clocks"].raw[:300]
+        print(json.dumps(line))
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-steps", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "stack"],
-                    help="decode = config 2 (the bench line); stack = config 4 (64 layers, head-sharded)")
+    ap.add_argument("--no-single", action="store_true", help="skip the config 0 / config 1 single-layer keys")
+    ap.add_argument("--no-stack", action="store_true", help="skip the config 4 stack key")
     ap.add_argument("--stack-ctx", type=int, default=131072)
     ap.add_argument("--stack-prefill", type=int, default=32768)
+    ap.add_argument("--stack-steps", type=int, default=10)
     ap.add_argument("--stack-prefill-iters", type=int, default=2)
     ap.add_argument("--prefill-iters", type=int, default=5)
-    ap.add_argument("--seqs", type=int, default=B_PER_RANK,
-                    help="sequences per GPU (default 64 = config 2; smaller only for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload == "stack":
-        return run_stack(args)
     return run_ours(args)
 
 
