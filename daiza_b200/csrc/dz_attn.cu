@@ -1,6 +1,7 @@
 // dz_attn.cu -- the C ABI (include/dz_attn.h): context, parameters, caches,
 // host-authoritative lengths/heads, and the compute entry points.
 #include <algorithm>
+#include <functional>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -240,6 +241,7 @@ int dz_last_launch_count(const dz_ctx* ctx) { return ctx ? ctx->last_launches : 
 dz_status dz_device_error(dz_ctx* ctx, int32_t* code) {
     if (!ctx || !code) return DZ_EINVAL;
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     DZ_CUDA(cudaDeviceSynchronize());
     int v = 0;
     DZ_CUDA(cudaMemcpy(&v, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -262,6 +264,7 @@ dz_status dz_layer_set_attn_params(dz_ctx* ctx, int layer, const float* q_norm, 
     LayerState& L = ctx->layers[layer];
     if (!L.is_attn) return fail(ctx, DZ_EINVAL, "layer %d is not a full-attention layer", layer);
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     dz_status st;
     if ((st = upload(ctx, &L.q_norm, q_norm, HD)) != DZ_OK) return st;
     if ((st = upload(ctx, &L.k_norm, k_norm, HD)) != DZ_OK) return st;
@@ -276,6 +279,7 @@ dz_status dz_layer_set_ssm_params(dz_ctx* ctx, int layer, const float* conv1d_t,
     LayerState& L = ctx->layers[layer];
     if (L.is_attn) return fail(ctx, DZ_EINVAL, "layer %d is not a Gated DeltaNet layer", layer);
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     dz_status st;
     if ((st = upload(ctx, &L.conv_w, conv1d_t, (size_t)CONV_K * QKV_LEN)) != DZ_OK) return st;
     if ((st = upload(ctx, &L.ssm_a, ssm_a, SSM_HV)) != DZ_OK) return st;
@@ -294,6 +298,7 @@ dz_status dz_cache_create(dz_ctx* ctx, int n_seqs, const int64_t* max_len) {
         max_cap = std::max(max_cap, max_len[s]);
     }
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     cudaDeviceSynchronize();
     free_cache(ctx);
     const int kvc = ctx->cfg.kv_head_count, vc = ctx->cfg.v_head_count;
@@ -350,12 +355,18 @@ dz_status dz_cache_create(dz_ctx* ctx, int n_seqs, const int64_t* max_len) {
     // decode scratch
     {
         void* d;
-        if ((st = dev_alloc(ctx, &d, (size_t)n_seqs * GRP * kvc * HD * sizeof(float), false)) != DZ_OK) {
+        const int nb = std::min(n_seqs, MAXB);   // sequences per decode launch
+        if ((st = dev_alloc(ctx, &d, (size_t)nb * GRP * kvc * HD * sizeof(float), false)) != DZ_OK) {
             free_cache(ctx);
             return st;
         }
         ctx->q_buf = static_cast<float*>(d);
-        ctx->part_items = (int64_t)std::min(n_seqs, MAXB) * kvc * MAXC;
+        // the nb largest caches bound the positions one launch reads
+        std::vector<int64_t> sorted(max_len, max_len + n_seqs);
+        std::sort(sorted.begin(), sorted.end(), std::greater<int64_t>());
+        int64_t sum_n = 0;
+        for (int s = 0; s < nb; ++s) sum_n += sorted[s];
+        ctx->part_items = decode_items_bound(ctx->n_sm, kvc, nb, sum_n);
         if ((st = dev_alloc(ctx, &d, (size_t)ctx->part_items * GRP * HD * sizeof(float), false)) != DZ_OK) {
             free_cache(ctx);
             return st;
@@ -391,6 +402,7 @@ dz_status dz_kv_truncate(dz_ctx* ctx, int layer, int seq, int64_t new_len) {
 dz_status dz_cache_reset(dz_ctx* ctx, int seq) {
     if (!ctx || seq < 0 || seq >= ctx->n_seqs) return fail(ctx, DZ_EINVAL, "bad seq");
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     const int vc = ctx->cfg.v_head_count;
     for (auto& L : ctx->layers) {
         if (L.is_attn) {
@@ -409,6 +421,7 @@ dz_status dz_kv_export(dz_ctx* ctx, int layer, int seq, float* k_flat, float* v_
     if (!layer_ok(ctx, layer) || !ctx->layers[layer].is_attn || seq < 0 || seq >= ctx->n_seqs || !k_flat || !v_flat)
         return fail(ctx, DZ_EINVAL, "bad export arguments");
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     const LayerState& L = ctx->layers[layer];
     const int kvc = ctx->cfg.kv_head_count;
     const int64_t n = L.len[seq];
@@ -431,6 +444,7 @@ dz_status dz_kv_import(dz_ctx* ctx, int layer, int seq, const float* k_flat, con
     if (len > L.h_kv[seq].cap) return fail(ctx, DZ_ESTATE, "import of %lld tokens exceeds capacity %lld",
                                            (long long)len, (long long)L.h_kv[seq].cap);
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     const int kvc = ctx->cfg.kv_head_count;
     for (int h = 0; h < kvc && len > 0; ++h) {
         DZ_CUDA(cudaMemcpy2D(L.h_kv[seq].k + (size_t)h * L.h_kv[seq].cap * HD, HD * 4, k_flat + (size_t)h * HD,
@@ -446,6 +460,7 @@ dz_status dz_ssm_export(dz_ctx* ctx, int layer, int seq, float* state, float* co
     if (!layer_ok(ctx, layer) || ctx->layers[layer].is_attn || seq < 0 || seq >= ctx->n_seqs)
         return fail(ctx, DZ_EINVAL, "bad ssm export arguments");
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     const LayerState& L = ctx->layers[layer];
     const int vc = ctx->cfg.v_head_count;
     if (state) DZ_CUDA(cudaMemcpy(state, L.h_ssm[seq].state, (size_t)vc * SSM_D * SSM_D * 4, cudaMemcpyDefault));
@@ -461,6 +476,7 @@ dz_status dz_ssm_import(dz_ctx* ctx, int layer, int seq, const float* state, con
         conv_head >= CONV_K)
         return fail(ctx, DZ_EINVAL, "bad ssm import arguments");
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     LayerState& L = ctx->layers[layer];
     const int vc = ctx->cfg.v_head_count;
     if (state) DZ_CUDA(cudaMemcpy(L.h_ssm[seq].state, state, (size_t)vc * SSM_D * SSM_D * 4, cudaMemcpyDefault));
@@ -476,6 +492,7 @@ dz_status dz_kv_fill_pattern(dz_ctx* ctx, int layer, int seq, int64_t len, int b
     LayerState& L = ctx->layers[layer];
     if (len > L.h_kv[seq].cap) return fail(ctx, DZ_ESTATE, "fill of %lld rows exceeds capacity", (long long)len);
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     const int kvc = ctx->cfg.kv_head_count;
     for (int h = 0; h < kvc && len > 0; ++h) {
         DZ_CUDA(cudaMemset(L.h_kv[seq].k + (size_t)h * L.h_kv[seq].cap * HD, byte_value, (size_t)len * HD * 4));
@@ -489,6 +506,7 @@ dz_status dz_rope_table(dz_ctx* ctx, int64_t pos0, int64_t n, float* out) {
     if (!ctx || !out || pos0 < 0 || n < 0 || pos0 + n > ctx->rope_n)
         return fail(ctx, DZ_EINVAL, "rope rows [%lld,%lld) outside table", (long long)pos0, (long long)(pos0 + n));
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     DZ_CUDA(cudaMemcpy(out, ctx->rope + pos0 * 2 * ROPE, (size_t)n * 2 * ROPE * 4, cudaMemcpyDeviceToHost));
     return DZ_OK;
 }
@@ -523,6 +541,9 @@ static dz_status gqa_decode_impl(dz_ctx* ctx, int layer, int B, const int32_t* s
             d.pos[b] = pos ? pos[b0 + b] : (int32_t)L.len[s];
             d.cum[b + 1] = d.cum[b] + (int32_t)((L.len[s] + 1 + chunk - 1) / chunk);
         }
+        if ((int64_t)d.cum[nb] * kvc > ctx->part_items)   // cannot happen under decode_items_bound
+            return fail(ctx, DZ_ESTATE, "gqa decode: %lld split-K items exceed the scratch (%lld)",
+                        (long long)d.cum[nb] * kvc, (long long)ctx->part_items);
         cudaError_t e = launch_gqa_decode(ctx, layer, d, q_gate + (size_t)b0 * nq * QG_ROW, k + (size_t)b0 * kvc * HD,
                                           v + (size_t)b0 * kvc * HD, out + (size_t)b0 * nq * HD, st, &launches);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "gqa decode launch");
@@ -578,6 +599,7 @@ dz_status dz_gqa_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_i
     if (st != DZ_OK) return st;
     if (!q_gate || !k || !v || !out) return fail(ctx, DZ_EINVAL, "null tensor");
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     const int kvc = ctx->cfg.kv_head_count, nq = GRP * kvc;
     const size_t nqg = (size_t)B * nq * QG_ROW, nk = (size_t)B * kvc * HD, no = (size_t)B * nq * HD;
     if ((st = ensure_stage(ctx, (nqg + 2 * nk + no) * 4)) != DZ_OK) return st;
@@ -632,6 +654,7 @@ dz_status dz_gdn_decode(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, c
     if (st != DZ_OK) return st;
     if (!qkv || !alpha || !beta || !z || !y) return fail(ctx, DZ_EINVAL, "null tensor");
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     return gdn_decode_impl(ctx, layer, B, seq_ids, qkv, alpha, beta, z, y, static_cast<cudaStream_t>(stream));
 }
 
@@ -641,6 +664,7 @@ dz_status dz_gdn_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_i
     if (st != DZ_OK) return st;
     if (!qkv || !alpha || !beta || !z || !y) return fail(ctx, DZ_EINVAL, "null tensor");
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     const int vc = ctx->cfg.v_head_count;
     const size_t nx = (size_t)B * QKV_LEN, na = (size_t)B * SSM_HV, nz = (size_t)B * INNER, ny = (size_t)B * vc * SSM_D;
     if ((st = ensure_stage(ctx, (nx + 2 * na + nz + ny) * 4)) != DZ_OK) return st;
@@ -729,6 +753,7 @@ dz_status dz_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float
     if (T <= 0) return fail(ctx, DZ_EINVAL, "T must be positive");
     if (!qkv || !alpha || !beta || !z || !y) return fail(ctx, DZ_EINVAL, "null tensor");
     DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     int launches = 0;
     cudaError_t e = launch_gdn_prefill(ctx, layer, seq, T, qkv, alpha, beta, z, y,
                                        static_cast<cudaStream_t>(stream), &launches);

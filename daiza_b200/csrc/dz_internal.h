@@ -10,7 +10,7 @@
 namespace dz {
 
 constexpr int MAXB = 256;   // sequences per kernel launch (descriptor rides in the kernel parameters)
-constexpr int MAXC = 128;   // max split-K chunks per (sequence, kv head) in decode
+constexpr int MAXC = 256;   // max split-K chunks per (sequence, kv head) in decode
 
 // One sequence's KV cache for one full-attention layer:
 //   k, v: [kv_head_count][cap][256] f32 -- per kv head a contiguous [seq, dim]
@@ -69,7 +69,7 @@ struct dz_ctx {
     int64_t rope_n = 0;
     std::vector<void*> cache_allocs;
     // decode scratch (owned by the context, sized at dz_cache_create)
-    float* q_buf = nullptr;     // [n_seqs][6*kvc][256]
+    float* q_buf = nullptr;     // [min(n_seqs, MAXB)][6*kvc][256] prepared q rows
     float* part_o = nullptr;    // [items][6][256] unnormalised split-K outputs
     float* part_ml = nullptr;   // [items][6][2]  (running max in log2 units, sum)
     int64_t part_items = 0;
@@ -80,7 +80,7 @@ struct dz_ctx {
     // prefill scratch (grown on demand)
     void* pf = nullptr;
     size_t pf_bytes = 0;
-    // Gated DeltaNet decode records (grown on demand)
+    // Gated DeltaNet decode records of the two-kernel decode path (grown on demand)
     float* gdn_rec = nullptr;
     size_t gdn_rec_bytes = 0;
 };
@@ -91,12 +91,27 @@ namespace dz {
 // (4 warps per SM) over the whole batch, 16..1024 positions, at most MAXC chunks
 // per (sequence, kv head), a multiple of 16.  total / nmax: sum and max of
 // len + 1 over the batch.
+#ifndef DZ_DECODE_CHUNK_MIN
+#define DZ_DECODE_CHUNK_MIN 16
+#endif
 inline int64_t decode_chunk(int n_sm, int kvc, int64_t total, int64_t nmax) {
     int64_t chunk = (total * kvc) / ((int64_t)n_sm * 16);
-    chunk = chunk < 16 ? 16 : (chunk > 1024 ? 1024 : chunk);
+    chunk = chunk < DZ_DECODE_CHUNK_MIN ? DZ_DECODE_CHUNK_MIN : (chunk > 1024 ? 1024 : chunk);
     const int64_t need = (nmax + MAXC - 1) / MAXC;
     if (chunk < need) chunk = need;
     return (chunk + 15) / 16 * 16;
+}
+
+// Upper bound on the split-K work items of one decode launch of at most B
+// sequences whose len + 1 sum to at most sum_n, under decode_chunk: the chunk
+// is at least floor(X) with X = total * kvc / (n_sm * 16) whenever X >= 16
+// (so total / chunk <= (17/16) n_sm * 16 / kvc), at least 16 when X < 16 (so
+// total / 16 < n_sm * 16 / kvc), or 1024 (total / 1024); and
+// sum_b ceil(n_b / chunk) <= total / chunk + B.  Twice the n_sm term keeps a
+// margin.
+inline int64_t decode_items_bound(int n_sm, int kvc, int64_t B, int64_t sum_n) {
+    const int64_t a = (int64_t)n_sm * 32, c = (sum_n * kvc + 1023) / 1024;
+    return (a > c ? a : c) + B * kvc;
 }
 
 // Makes `dev` current for the lifetime of the guard and restores the caller's

@@ -2,18 +2,21 @@
 //
 // Reference: Daiza-engine/src/model/attention.rs:90-203 (one token per
 // sequence).  Three stream-ordered kernels:
-//   1. gqa_prep     : per sequence -- deinterleave [Q_h|gate_h], QK-RMSNorm,
-//                     partial RoPE (the reference's '+' sign, math/rope.rs:205-210)
-//                     at pos = len, q *= 1/16, append K/V at slot len.
+//   1. gqa_prep     : per sequence and head -- deinterleave [Q_h|gate_h],
+//                     QK-RMSNorm, partial RoPE (the reference's '+' sign,
+//                     math/rope.rs:205-210), q *= 1/16 -> q_buf; append K/V at
+//                     slot len.
 //   2. gqa_split    : per (sequence, split-K chunk, kv head), one warp each --
 //                     the 6 grouped q heads attend over the chunk's cached
 //                     positions.  K/V tiles of 8 positions stream HBM -> shared
 //                     memory through 1-D bulk async copies (cp.async.bulk +
 //                     mbarrier, 3 stages per warp); scores on the FP32 pipes
 //                     with a warp-shuffle reduce-scatter, online softmax in
-//                     log2 units, unnormalised partials out.
-//   3. gqa_combine  : per (sequence, kv head) -- merge the chunks' (m, l, o),
-//                     divide, multiply by sigmoid(gate).
+//                     log2 units, unnormalised partials out.  A programmatic
+//                     dependent of 1: old K/V tiles stream in while 1 finishes.
+//   3. gqa_combine  : per (q head, sequence), a programmatic dependent of 2 --
+//                     merge the chunks' (m, l, o), divide, multiply by
+//                     sigmoid(gate).
 // Memory bound: every cached K and V byte is read exactly once.
 #include <algorithm>
 #include <cstddef>
@@ -25,8 +28,38 @@ namespace dz {
 constexpr int STAGES = 3;
 
 // ---------------------------------------------------------------------------
-// 1. prep: 8 warps, one head task per warp-iteration.  tasks [0, nq) are q heads,
-//    [nq, nq+kvc) are kv heads.  Lane l holds dims [4l,4l+4) and [128+4l,128+4l+4).
+// Per-head prologue (attention.rs:92-113) on a loaded head row: RMSNorm
+// (rmsnorm.rs:284, (x*inv)*w), partial RoPE on dims [0, 64) with the reference's
+// '+' sign for both halves (math/rope.rs:205-210), then the scale (1/sqrt(256)
+// for q, 1 for k).  One warp per head row of 256; lane l holds dims [4l,4l+4)
+// (x0) and [128+4l,128+4l+4) (x1); c/sn are the RoPE cos/sin of dims [4l,4l+4)
+// (lanes 0..15).  The partner of dim i < 32 is i + 32, i.e. lane ^ 8.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void norm_rope(float4& x0, float4& x1, const float4 w0, const float4 w1, const float4 c,
+                                          const float4 sn, float eps, float scale, int lane) {
+    float ss = x0.x * x0.x + x0.y * x0.y + x0.z * x0.z + x0.w * x0.w +
+               x1.x * x1.x + x1.y * x1.y + x1.z * x1.z + x1.w * x1.w;
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)HD + eps);
+    x0 = make_float4((x0.x * inv) * w0.x, (x0.y * inv) * w0.y, (x0.z * inv) * w0.z, (x0.w * inv) * w0.w);
+    x1 = make_float4((x1.x * inv) * w1.x, (x1.y * inv) * w1.y, (x1.z * inv) * w1.z, (x1.w * inv) * w1.w);
+    float4 pr;
+    pr.x = __shfl_xor_sync(0xffffffffu, x0.x, 8);
+    pr.y = __shfl_xor_sync(0xffffffffu, x0.y, 8);
+    pr.z = __shfl_xor_sync(0xffffffffu, x0.z, 8);
+    pr.w = __shfl_xor_sync(0xffffffffu, x0.w, 8);
+    if (lane < 16)   // cos[i] == cos[i^32]; out = x*c + partner*s for both halves
+        x0 = make_float4(fmaf(x0.x, c.x, pr.x * sn.x), fmaf(x0.y, c.y, pr.y * sn.y),
+                         fmaf(x0.z, c.z, pr.z * sn.z), fmaf(x0.w, c.w, pr.w * sn.w));
+    if (scale != 1.0f) {
+        x0 = make_float4(x0.x * scale, x0.y * scale, x0.z * scale, x0.w * scale);
+        x1 = make_float4(x1.x * scale, x1.y * scale, x1.z * scale, x1.w * scale);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 1. gqa_prep: grid (B, ceil((nq + kvc) / 8)), one head task per warp.  Tasks [0, nq) are q heads -> q_buf; [nq, nq + kvc) are kv
+//    heads: K (normed, RoPE'd) and V appended at slot len (kv_cache.rs:79-88).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) gqa_prep_kernel(GqaDecodeDesc d, int kvc, const KvSlot* __restrict__ kv,
                                                        const float* __restrict__ q_norm,
@@ -36,64 +69,41 @@ __global__ void __launch_bounds__(256) gqa_prep_kernel(GqaDecodeDesc d, int kvc,
                                                        const float* __restrict__ k_in,
                                                        const float* __restrict__ v_in,
                                                        float* __restrict__ q_buf, float eps) {
+    // the split grid may launch now: it streams old K/V tiles and waits for this
+    // grid before it reads q_buf or the appended row
+    asm volatile("griddepcontrol.launch_dependents;");
     const int b = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int sid = d.sid[b];
-    const int pos = d.len[b];                      // cache slot (kv_cache.rs:79-88)
     const int nq = GRP * kvc;
-    const KvSlot slot = kv[sid];
+    const int task = blockIdx.y * 8 + warp;
+    if (task >= nq + kvc) return;
     const float* cs = rope + (size_t)d.pos[b] * (2 * ROPE);   // RoPE row of ModelState::pos (forward.rs:230-238)
-    for (int task = warp; task < nq + kvc; task += 8) {
-        const float* src;
-        const float* w;
-        float* dst;
-        float scale;
-        if (task < nq) {
-            src = q_gate + ((size_t)b * nq + task) * QG_ROW;
-            w = q_norm;
-            dst = q_buf + ((size_t)b * nq + task) * HD;
-            scale = 0.0625f;                     // 1/sqrt(256), attention.rs:110
-        } else {
-            const int h = task - nq;
-            src = k_in + ((size_t)b * kvc + h) * HD;
-            w = k_norm;
-            dst = slot.k + ((size_t)h * slot.cap + pos) * HD;
-            scale = 1.0f;
-            // V is appended unchanged (kv_cache.rs:79-88)
-            const float* vs = v_in + ((size_t)b * kvc + h) * HD;
-            float* vd = slot.v + ((size_t)h * slot.cap + pos) * HD;
-            reinterpret_cast<float4*>(vd)[lane] = reinterpret_cast<const float4*>(vs)[lane];
-            reinterpret_cast<float4*>(vd)[lane + 32] = reinterpret_cast<const float4*>(vs)[lane + 32];
-        }
-        float4 x0 = reinterpret_cast<const float4*>(src)[lane];
-        float4 x1 = reinterpret_cast<const float4*>(src)[lane + 32];
-        float ss = x0.x * x0.x + x0.y * x0.y + x0.z * x0.z + x0.w * x0.w +
-                   x1.x * x1.x + x1.y * x1.y + x1.z * x1.z + x1.w * x1.w;
-        ss = warp_sum(ss);
-        const float inv = 1.0f / sqrtf(ss / (float)HD + eps);     // rmsnorm.rs:284
-        const float4 w0 = reinterpret_cast<const float4*>(w)[lane];
-        const float4 w1 = reinterpret_cast<const float4*>(w)[lane + 32];
-        x0 = make_float4((x0.x * inv) * w0.x, (x0.y * inv) * w0.y, (x0.z * inv) * w0.z, (x0.w * inv) * w0.w);
-        x1 = make_float4((x1.x * inv) * w1.x, (x1.y * inv) * w1.y, (x1.z * inv) * w1.z, (x1.w * inv) * w1.w);
-        // partial RoPE on dims [0,64): lanes 0..15 hold them; partner of dim i is i^32 (lane ^ 8)
-        float4 pr;
-        pr.x = __shfl_xor_sync(0xffffffffu, x0.x, 8);
-        pr.y = __shfl_xor_sync(0xffffffffu, x0.y, 8);
-        pr.z = __shfl_xor_sync(0xffffffffu, x0.z, 8);
-        pr.w = __shfl_xor_sync(0xffffffffu, x0.w, 8);
-        if (lane < 16) {
-            const float4 c = reinterpret_cast<const float4*>(cs)[lane];          // cos[i] == cos[i^32]
-            const float4 s = reinterpret_cast<const float4*>(cs + ROPE)[lane];
-            // out = x*c + partner*s   (both halves use '+', math/rope.rs:205-210)
-            x0 = make_float4(fmaf(x0.x, c.x, pr.x * s.x), fmaf(x0.y, c.y, pr.y * s.y),
-                             fmaf(x0.z, c.z, pr.z * s.z), fmaf(x0.w, c.w, pr.w * s.w));
-        }
-        if (scale != 1.0f) {
-            x0 = make_float4(x0.x * scale, x0.y * scale, x0.z * scale, x0.w * scale);
-            x1 = make_float4(x1.x * scale, x1.y * scale, x1.z * scale, x1.w * scale);
-        }
-        reinterpret_cast<float4*>(dst)[lane] = x0;
-        reinterpret_cast<float4*>(dst)[lane + 32] = x1;
+    const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 rc = lane < 16 ? reinterpret_cast<const float4*>(cs)[lane] : zero4;
+    const float4 rs = lane < 16 ? reinterpret_cast<const float4*>(cs + ROPE)[lane] : zero4;
+    if (task < nq) {
+        const float4* src = reinterpret_cast<const float4*>(q_gate + ((size_t)b * nq + task) * QG_ROW);
+        float4 x0 = src[lane], x1 = src[lane + 32];
+        norm_rope(x0, x1, reinterpret_cast<const float4*>(q_norm)[lane],
+                  reinterpret_cast<const float4*>(q_norm)[lane + 32], rc, rs, eps, 0.0625f, lane);
+        float4* dst = reinterpret_cast<float4*>(q_buf + ((size_t)b * nq + task) * HD);
+        dst[lane] = x0;
+        dst[lane + 32] = x1;
+    } else {
+        const int h = task - nq;
+        const KvSlot slot = kv[d.sid[b]];
+        const float4* ks = reinterpret_cast<const float4*>(k_in + ((size_t)b * kvc + h) * HD);
+        const float4* vs = reinterpret_cast<const float4*>(v_in + ((size_t)b * kvc + h) * HD);
+        float4 x0 = ks[lane], x1 = ks[lane + 32];
+        const float4 v0 = vs[lane], v1 = vs[lane + 32];
+        norm_rope(x0, x1, reinterpret_cast<const float4*>(k_norm)[lane],
+                  reinterpret_cast<const float4*>(k_norm)[lane + 32], rc, rs, eps, 1.0f, lane);
+        float4* kd = reinterpret_cast<float4*>(slot.k + ((size_t)h * slot.cap + d.len[b]) * HD);
+        float4* vd = reinterpret_cast<float4*>(slot.v + ((size_t)h * slot.cap + d.len[b]) * HD);
+        kd[lane] = x0;
+        kd[lane + 32] = x1;
+        vd[lane] = v0;
+        vd[lane + 32] = v1;
     }
 }
 
@@ -188,13 +198,25 @@ __global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaDecodeDesc d, int 
     }
     __syncwarp();
 
+    // the combine grid may launch now; it waits for this grid before reading partials
+    asm volatile("griddepcontrol.launch_dependents;");
     // producer cursor (lane 0 issues, all lanes track it uniformly)
     int p_item = gw, p_tile = 0;
     ItemInfo pinfo{};
     if (p_item < n_items) pinfo = decode_item(d, kvc, kv, p_item);
+    // gqa_prep (the programmatic predecessor) appends the row at slot len, so a
+    // tile that holds it is requested only after the grid-dependency wait
+    bool dep_done = false;
+    auto wait_prep = [&]() {
+        if (!dep_done) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            dep_done = true;
+        }
+    };
     auto produce = [&](int stage) {
         if (p_item >= n_items) return;
         const int rows = min(TP, pinfo.p1 - (pinfo.p0 + p_tile * TP));
+        if (pinfo.p0 + p_tile * TP + rows > d.len[pinfo.b]) wait_prep();
         if (lane == 0) {
             mbar_arrive_expect_tx(&R.full[stage], (uint32_t)rows * HD * 4 * 2);
             bulk_g2s(&R.k[stage][0][0], pinfo.kb + (size_t)p_tile * TP * HD, (uint32_t)rows * HD * 4, &R.full[stage]);
@@ -207,6 +229,7 @@ __global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaDecodeDesc d, int 
         }
     };
     for (int s = 0; s < STAGES; ++s) produce(s);
+    wait_prep();   // q_buf comes from gqa_prep
 
     const int k_grp = lane >> 1;              // reduce-scatter group: indices 3k..3k+2 of (pos*6 + head)
     const int my_pos = k_grp >> 1;
@@ -335,78 +358,117 @@ __global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaDecodeDesc d, int 
 }
 
 // ---------------------------------------------------------------------------
-// 3. combine chunks, normalise, gate.  grid (kvc, B), 256 threads (one dim each)
+// 3. combine chunks, normalise, gate.  One CTA per (q head, sequence) of
+//    32 * G threads (G = 8, 16 or 32 chunk groups, enough threads for one
+//    (m, l) pair each): group g sums chunks g, g + G, ... with lane l owning
+//    dims [4l,4l+4) and [128+4l,128+4l+4); the G group sums meet in shared
+//    memory.  Launched as a programmatic dependent of the split grid.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) gqa_combine_kernel(GqaDecodeDesc d, int kvc, const float* __restrict__ part_o,
-                                                          const float* __restrict__ part_ml,
-                                                          const float* __restrict__ q_gate,
-                                                          float* __restrict__ out) {
-    __shared__ float wgt[MAXC][GRP];
-    __shared__ float invl[GRP];
-    const int kvh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-    const int c0 = d.cum[b], nc = d.cum[b + 1] - d.cum[b];
-    if (tid < GRP) {
-        float M = -INFINITY;
-        for (int c = 0; c < nc; ++c)
-            M = fmaxf(M, part_ml[(((size_t)(c0 + c) * kvc + kvh) * GRP + tid) * 2]);
-        float L = 0.0f;
-        for (int c = 0; c < nc; ++c) {
-            const size_t it = ((size_t)(c0 + c) * kvc + kvh) * GRP + tid;
-            const float w = exp2f(part_ml[it * 2] - M);
-            wgt[c][tid] = w;
-            L = fmaf(part_ml[it * 2 + 1], w, L);
-        }
-        invl[tid] = 1.0f / L;
-    }
-    __syncthreads();
+constexpr int CMB_MAX_GROUPS = 32;
+static_assert(MAXC <= 32 * CMB_MAX_GROUPS, "one (m, l) pair per thread");
+__global__ void __launch_bounds__(32 * CMB_MAX_GROUPS) gqa_combine_kernel(GqaDecodeDesc d, int kvc,
+                                                                          const float* __restrict__ part_o,
+                                                                          const float* __restrict__ part_ml,
+                                                                          const float* __restrict__ q_gate,
+                                                                          float* __restrict__ out) {
+    __shared__ float wgt[MAXC];
+    __shared__ float red[2][CMB_MAX_GROUPS];
+    __shared__ __align__(16) float acc_s[CMB_MAX_GROUPS][HD];
     const int nq = GRP * kvc;
-#pragma unroll
-    for (int h = 0; h < GRP; ++h) {
-        float acc = 0.0f;
-        for (int c = 0; c < nc; ++c)
-            acc = fmaf(part_o[((size_t)(c0 + c) * kvc + kvh) * GRP * HD + h * HD + tid], wgt[c][h], acc);
-        const int qh = kvh * GRP + h;
-        const float g = q_gate[((size_t)b * nq + qh) * QG_ROW + HD + tid];
-        out[((size_t)b * nq + qh) * HD + tid] = acc * invl[h] * sigmoidf_acc(g);
+    const int qh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int kvh = qh / GRP, h = qh - kvh * GRP;
+    const int warp = tid >> 5, lane = tid & 31, groups = blockDim.x >> 5;
+    // an input, readable before the grid-dependency wait
+    const float gate = tid < HD ? q_gate[((size_t)b * nq + qh) * QG_ROW + HD + tid] : 0.0f;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int c0 = d.cum[b], nc = d.cum[b + 1] - d.cum[b];   // nc <= blockDim.x
+    float m = -INFINITY, l = 0.0f;
+    if (tid < nc) {
+        const float2 ml = *reinterpret_cast<const float2*>(part_ml + (((size_t)(c0 + tid) * kvc + kvh) * GRP + h) * 2);
+        m = ml.x;
+        l = ml.y;
+    }
+    const float wm = warp_max(m);
+    if (lane == 0) red[0][warp] = wm;
+    __syncthreads();
+    float M = red[0][0];
+    for (int w = 1; w < groups; ++w) M = fmaxf(M, red[0][w]);
+    float lw = 0.0f;
+    if (tid < nc) {
+        const float w = exp2f(m - M);
+        wgt[tid] = w;
+        lw = l * w;
+    }
+    lw = warp_sum(lw);
+    if (lane == 0) red[1][warp] = lw;
+    __syncthreads();
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    const float* base = part_o + (size_t)h * HD + 4 * lane;
+#pragma unroll 4
+    for (int c = warp; c < nc; c += groups) {
+        const float* po = base + ((size_t)(c0 + c) * kvc + kvh) * GRP * HD;
+        const float4 x0 = *reinterpret_cast<const float4*>(po);
+        const float4 x1 = *reinterpret_cast<const float4*>(po + 128);
+        const float w = wgt[c];
+        a0.x = fmaf(x0.x, w, a0.x); a0.y = fmaf(x0.y, w, a0.y); a0.z = fmaf(x0.z, w, a0.z); a0.w = fmaf(x0.w, w, a0.w);
+        a1.x = fmaf(x1.x, w, a1.x); a1.y = fmaf(x1.y, w, a1.y); a1.z = fmaf(x1.z, w, a1.z); a1.w = fmaf(x1.w, w, a1.w);
+    }
+    *reinterpret_cast<float4*>(&acc_s[warp][4 * lane]) = a0;
+    *reinterpret_cast<float4*>(&acc_s[warp][128 + 4 * lane]) = a1;
+    __syncthreads();
+    if (tid < HD) {
+        float L = 0.0f;
+        for (int w = 0; w < groups; ++w) L += red[1][w];
+        float o = 0.0f;
+        for (int g = 0; g < groups; ++g) o += acc_s[g][tid];
+        out[((size_t)b * nq + qh) * HD + tid] = o * (1.0f / L) * sigmoidf_acc(gate);
     }
 }
 
-cudaError_t launch_gqa_decode(dz_ctx* ctx, int layer, const GqaDecodeDesc& d, const float* q_gate,
-                              const float* k, const float* v, float* out, cudaStream_t st, int* n_launch) {
-    const LayerState& L = ctx->layers[layer];
-    const int kvc = ctx->cfg.kv_head_count;
-    const int items = d.cum[d.B] * kvc;
-    cudaFuncSetAttribute(gqa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SplitSmem));
-    gqa_prep_kernel<<<d.B, 256, 0, st>>>(d, kvc, L.d_kv, L.q_norm, L.k_norm, ctx->rope, q_gate, k, v, ctx->q_buf,
-                                         ctx->cfg.rms_eps);
-    const int grid = std::min((items + NWARP - 1) / NWARP, ctx->n_sm);
-    gqa_split_kernel<<<grid, 32 * NWARP, sizeof(SplitSmem), st>>>(d, kvc, L.d_kv, ctx->q_buf, ctx->part_o,
-                                                                  ctx->part_ml, ctx->d_err, items);
-    gqa_combine_kernel<<<dim3(kvc, d.B), 256, 0, st>>>(d, kvc, ctx->part_o, ctx->part_ml, q_gate, out);
-    *n_launch += 3;
-    return cudaGetLastError();
-}
-
-}  // namespace dz
-
-namespace dz {
-// Same three launches as launch_gqa_decode, with the split-K scratch supplied by
-// the caller instead of taken from the context (used by the no-allocation entry
-// point, whose scratch is a fixed device array).
+// prep (plain launch: it follows whatever came before in the stream), then the
+// split grid as a programmatic dependent of prep (old K/V tiles stream in while
+// prep finishes) and the combine grid as a programmatic dependent of split.
 cudaError_t launch_gqa_decode_scratch(dz_ctx* ctx, int layer, const GqaDecodeDesc& d, const float* q_gate,
                                       const float* k, const float* v, float* out, cudaStream_t st, int* n_launch,
                                       float* q_buf, float* part_o, float* part_ml) {
     const LayerState& L = ctx->layers[layer];
     const int kvc = ctx->cfg.kv_head_count;
     const int items = d.cum[d.B] * kvc;
-    cudaFuncSetAttribute(gqa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SplitSmem));
-    gqa_prep_kernel<<<d.B, 256, 0, st>>>(d, kvc, L.d_kv, L.q_norm, L.k_norm, ctx->rope, q_gate, k, v, q_buf,
-                                         ctx->cfg.rms_eps);
-    const int grid = std::min((items + NWARP - 1) / NWARP, ctx->n_sm);
-    gqa_split_kernel<<<grid, 32 * NWARP, sizeof(SplitSmem), st>>>(d, kvc, L.d_kv, q_buf, part_o, part_ml,
-                                                                  ctx->d_err, items);
-    gqa_combine_kernel<<<dim3(kvc, d.B), 256, 0, st>>>(d, kvc, part_o, part_ml, q_gate, out);
+    int max_nc = 0;
+    for (int b = 0; b < d.B; ++b) max_nc = std::max(max_nc, d.cum[b + 1] - d.cum[b]);
+    cudaError_t e = cudaFuncSetAttribute(gqa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(SplitSmem));
+    if (e != cudaSuccess) return e;
+    gqa_prep_kernel<<<dim3(d.B, (GRP * kvc + kvc + 7) / 8), 256, 0, st>>>(d, kvc, L.d_kv, L.q_norm, L.k_norm,
+                                                                          ctx->rope, q_gate, k, v, q_buf,
+                                                                          ctx->cfg.rms_eps);
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(std::min((items + NWARP - 1) / NWARP, ctx->n_sm));
+    lc.blockDim = dim3(32 * NWARP);
+    lc.dynamicSmemBytes = sizeof(SplitSmem);
+    lc.stream = st;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&lc, gqa_split_kernel, d, kvc, (const KvSlot*)L.d_kv, (const float*)q_buf, part_o,
+                           part_ml, ctx->d_err, items);
+    if (e != cudaSuccess) return e;
+    const int groups = max_nc > 256 / 2 ? 32 : (max_nc > 64 ? 16 : 8);
+    lc.gridDim = dim3(GRP * kvc, d.B);
+    lc.blockDim = dim3(32 * groups);
+    lc.dynamicSmemBytes = 0;
+    e = cudaLaunchKernelEx(&lc, gqa_combine_kernel, d, kvc, (const float*)part_o, (const float*)part_ml, q_gate, out);
+    if (e != cudaSuccess) return e;
     *n_launch += 3;
     return cudaGetLastError();
 }
+
+cudaError_t launch_gqa_decode(dz_ctx* ctx, int layer, const GqaDecodeDesc& d, const float* q_gate,
+                              const float* k, const float* v, float* out, cudaStream_t st, int* n_launch) {
+    return launch_gqa_decode_scratch(ctx, layer, d, q_gate, k, v, out, st, n_launch, ctx->q_buf, ctx->part_o,
+                                     ctx->part_ml);
+}
+
 }  // namespace dz

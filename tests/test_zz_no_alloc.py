@@ -104,7 +104,7 @@ def _decode_chunk(n_sm, kvc, lens):
     total, nmax = int(sum(n + 1 for n in lens)), int(max(n + 1 for n in lens))
     chunk = (total * kvc) // (n_sm * 16)
     chunk = min(max(chunk, 16), 1024)
-    chunk = max(chunk, -(-nmax // 128))
+    chunk = max(chunk, -(-nmax // 256))
     return -(-chunk // 16) * 16
 
 
