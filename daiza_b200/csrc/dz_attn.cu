@@ -208,6 +208,13 @@ dz_status dz_ctx_create(int device, const dz_config* cfg, dz_ctx** out) {
         delete ctx;
         return DZ_ENOMEM;
     }
+    bool ok = cudaStreamCreateWithFlags(&ctx->pf_side, cudaStreamNonBlocking) == cudaSuccess;
+    for (auto& e : ctx->pf_ev) ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        dz_ctx_destroy(ctx);
+        return DZ_ECUDA;
+    }
     *out = ctx;
     return DZ_OK;
 }
@@ -225,6 +232,9 @@ dz_status dz_ctx_destroy(dz_ctx* ctx) {
         if (ctx->pf) cudaFree(ctx->pf);
         if (ctx->gdn_rec) cudaFree(ctx->gdn_rec);
         if (ctx->d_err) cudaFree(ctx->d_err);
+        for (auto& e : ctx->pf_ev)
+            if (e) cudaEventDestroy(e);
+        if (ctx->pf_side) cudaStreamDestroy(ctx->pf_side);
     }
     delete ctx;
     return DZ_OK;

@@ -11,6 +11,7 @@ namespace dz {
 
 constexpr int MAXB = 256;   // sequences per kernel launch (descriptor rides in the kernel parameters)
 constexpr int MAXC = 256;   // max split-K chunks per (sequence, kv head) in decode
+constexpr int PF_MAX_SEGMENTS = 16;   // chunk segments of a pipelined Gated DeltaNet prefill
 
 // One sequence's KV cache for one full-attention layer:
 //   k, v: [kv_head_count][cap][256] f32 -- per kv head a contiguous [seq, dim]
@@ -83,6 +84,10 @@ struct dz_ctx {
     // Gated DeltaNet decode records of the two-kernel decode path (grown on demand)
     float* gdn_rec = nullptr;
     size_t gdn_rec_bytes = 0;
+    // Gated DeltaNet prefill: side stream of the intra-chunk kernels and the events
+    // that order them with the chain kernels (created with the context)
+    cudaStream_t pf_side = nullptr;
+    cudaEvent_t pf_ev[dz::PF_MAX_SEGMENTS + 1] = {};
 };
 
 namespace dz {

@@ -191,7 +191,7 @@ constexpr uint32_t I_KQ = 0, I_W = 64, I_U0 = 128;
 __global__ void __launch_bounds__(256, 1) gdn_pf_intra_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                               const __grid_constant__ CUtensorMap tm_k,
                                                               const __grid_constant__ CUtensorMap tm_v, int64_t Tp,
-                                                              int n_items, int vh0, int vc,
+                                                              int item0, int n_items, int vh0, int vc,
                                                               const float* __restrict__ gl,
                                                               const float* __restrict__ bt,
                                                               unsigned char* __restrict__ rec, int* err) {
@@ -233,13 +233,13 @@ __global__ void __launch_bounds__(256, 1) gdn_pf_intra_kernel(const __grid_const
         bulk_g2s(sm.g[b], gl + (size_t)vl * Tp + t0, 256, &sm.bar_kq[b]);
         bulk_g2s(sm.b[b], bt + (size_t)vl * Tp + t0, 256, &sm.bar_kq[b]);
     };
-    if (tid == 0 && (int)blockIdx.x < n_items) load_kq(blockIdx.x, 0);
+    if (tid == 0 && item0 + (int)blockIdx.x < n_items) load_kq(item0 + blockIdx.x, 0);
 
     const int q4 = warp & 3, h = warp >> 2;
     const int row = 32 * q4 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q4) << 16);
     int n = 0;
-    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++n) {
+    for (int i = item0 + blockIdx.x; i < n_items && ok; i += gridDim.x, ++n) {
         const int buf = n & 1;
         const int c = i / vc, vl = i % vc, kh = (vh0 + vl) % SSM_HK;
         unsigned char* R = rec + ((size_t)c * vc + vl) * REC_BYTES;
@@ -582,7 +582,7 @@ __device__ __forceinline__ void load_u0(const unsigned char* rec_u0, int v, int 
 
 __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-    const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_y, int64_t T, int NC, int vh0,
+    const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_y, int c0, int NC, int vh0,
     int vc, const unsigned char* __restrict__ rec, float* __restrict__ state, const float* __restrict__ norm_w, int* err) {
     using namespace gp;
     using namespace tc;
@@ -591,7 +591,8 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
     const int vl = blockIdx.x, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int kh = (vh0 + vl) % SSM_HK;
-    auto R = [&](int c) { return rec + ((size_t)c * vc + vl) * REC_BYTES; };
+    // chunks c0 .. c0 + NC - 1 of the sequence; loop counters below are local (0 .. NC - 1)
+    auto R = [&](int c) { return rec + ((size_t)(c0 + c) * vc + vl) * REC_BYTES; };
 
     if (warp == MMA_W) tmem_alloc(&sm.tmem_base, 512);
     if (tid == 0) {
@@ -636,7 +637,7 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
             for (int c = 0; c < NC && ok; ++c) {
                 const int b = c & 1;
                 const uint32_t pp2 = (uint32_t)(((c - 2) >> 1) & 1);
-                const int t0 = c * C;
+                const int t0 = (c0 + c) * C;
                 // K(c) -> KD[b]
                 if (c > 1 && !wait_or_flag(&sm.mma3_done[b], pp2, err, ok)) break;
                 mbar_arrive_expect_tx(&sm.full_k[b], 32768);
@@ -648,7 +649,7 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
                     const int bp = (c - 1) & 1;
                     if (!wait_or_flag(&sm.mma1_done[bp], (uint32_t)(((c - 1) >> 1) & 1), err, ok)) break;
                     mbar_arrive_expect_tx(&sm.full_z[bp], C * D * 4);
-                    tma_load_2d(sm.wq[bp], &tm_z, (vh0 + vl) * D, (c - 1) * C, &sm.full_z[bp]);
+                    tma_load_2d(sm.wq[bp], &tm_z, (vh0 + vl) * D, (c0 + c - 1) * C, &sm.full_z[bp]);
                 }
                 // G(c+5) into the slot of chunk c-3, whose last reader (the y epilogue) was done
                 // before MMA1(c-2)
@@ -676,7 +677,7 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
                 const int bp = (NC - 1) & 1;
                 if (wait_or_flag(&sm.mma1_done[bp], (uint32_t)(((NC - 1) >> 1) & 1), err, ok)) {
                     mbar_arrive_expect_tx(&sm.full_z[bp], C * D * 4);
-                    tma_load_2d(sm.wq[bp], &tm_z, (vh0 + vl) * D, (NC - 1) * C, &sm.full_z[bp]);
+                    tma_load_2d(sm.wq[bp], &tm_z, (vh0 + vl) * D, (c0 + NC - 1) * C, &sm.full_z[bp]);
                 }
             }
         }
@@ -944,7 +945,7 @@ __global__ void __launch_bounds__(gp::CHAIN_THREADS, 1) gdn_pf_chain_kernel(
             tc::named_bar_sync(BAR_EY, 256);
             if (tid == 0) {
                 // rows past T are clipped by the tensor store
-                tma_store_2d(&tm_y, vl * D, c * C, yt);
+                tma_store_2d(&tm_y, vl * D, (c0 + c) * C, yt);
                 bulk_commit();
                 bulk_wait_read_all();
                 mbar_arrive(&sm.wq_free[b]);
@@ -986,6 +987,31 @@ bool make_rows_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Chunk segments of the pipelined prefill, as boundaries b[0] = 0 < ... < b[n] = NC.
+// One segment when the sequence is short (under 16 chunks) or the chain kernels
+// would leave too few SMs for the intra-chunk kernels.  Otherwise the segments
+// grow from the end backwards (NC/16, doubling, at most NC/4): the chain work
+// of the last segment is the only part not overlapped with intra-chunk work.
+int pf_segments(int NC, int vc, int n_sm, int* b) {
+    b[0] = 0;
+    if (NC < 16 || 2 * vc > n_sm) {
+        b[1] = NC;
+        return 1;
+    }
+    int sizes[PF_MAX_SEGMENTS];
+    int n = 0, rem = NC, sz = std::max(2, NC / 16);
+    const int cap = std::max(sz, NC / 4);
+    while (rem > 0 && n < PF_MAX_SEGMENTS) {
+        const int take = std::min(sz, rem);
+        sizes[n++] = take;
+        rem -= take;
+        sz = std::min(2 * sz, cap);
+    }
+    sizes[n - 1] += rem;   // whatever is left joins the first segment
+    for (int k = 0; k < n; ++k) b[k + 1] = b[k] + sizes[n - 1 - k];
+    return n;
+}
 }  // namespace
 
 cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* qkv, const float* alpha,
@@ -1023,15 +1049,40 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
     const int smem_i = (int)sizeof(IntraSmem) + 1024;
     e = cudaFuncSetAttribute(gdn_pf_intra_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_i);
     if (e != cudaSuccess) return e;
-    const int n_items = NC * vc;
-    gdn_pf_intra_kernel<<<std::min(n_items, ctx->n_sm), 256, smem_i, st>>>(mq, mk, mv, Tp, n_items, vh0, vc, gl, bt,
-                                                                          rec, ctx->d_err);
     const int smem_c = (int)sizeof(ChainSmem) + 1024;
     e = cudaFuncSetAttribute(gdn_pf_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_c);
     if (e != cudaSuccess) return e;
-    gdn_pf_chain_kernel<<<vc, CHAIN_THREADS, smem_c, st>>>(mq, mk, mz, my, T, NC, vh0, vc, rec, slot.state, L.norm_w,
-                                                           ctx->d_err);
-    *n_launch += 4;
+    int bounds[PF_MAX_SEGMENTS + 1];
+    const int nseg = pf_segments(NC, vc, ctx->n_sm, bounds);
+    if (nseg == 1) {
+        const int n_items = NC * vc;
+        gdn_pf_intra_kernel<<<std::min(n_items, ctx->n_sm), 256, smem_i, st>>>(mq, mk, mv, Tp, 0, n_items, vh0, vc, gl,
+                                                                              bt, rec, ctx->d_err);
+        gdn_pf_chain_kernel<<<vc, CHAIN_THREADS, smem_c, st>>>(mq, mk, mz, my, 0, NC, vh0, vc, rec, slot.state,
+                                                               L.norm_w, ctx->d_err);
+        *n_launch += 4;
+        return cudaGetLastError();
+    }
+    // Pipelined: the intra-chunk kernels of segment k + 1 (side stream, n_sm - vc
+    // CTAs) run while the chain kernel of segment k (this stream, vc CTAs) runs on
+    // the other SMs.  Only stream order and events connect them; no kernel waits
+    // on another.
+    cudaStream_t side = ctx->pf_side;
+    if ((e = cudaEventRecord(ctx->pf_ev[0], st)) != cudaSuccess) return e;
+    if ((e = cudaStreamWaitEvent(side, ctx->pf_ev[0], 0)) != cudaSuccess) return e;
+    const int grid_i = ctx->n_sm - vc;
+    for (int k = 0; k < nseg; ++k) {
+        const int i0 = bounds[k] * vc, i1 = bounds[k + 1] * vc;
+        gdn_pf_intra_kernel<<<std::min(i1 - i0, grid_i), 256, smem_i, side>>>(mq, mk, mv, Tp, i0, i1, vh0, vc, gl, bt,
+                                                                             rec, ctx->d_err);
+        if ((e = cudaEventRecord(ctx->pf_ev[k + 1], side)) != cudaSuccess) return e;
+    }
+    for (int k = 0; k < nseg; ++k) {
+        if ((e = cudaStreamWaitEvent(st, ctx->pf_ev[k + 1], 0)) != cudaSuccess) return e;
+        gdn_pf_chain_kernel<<<vc, CHAIN_THREADS, smem_c, st>>>(mq, mk, mz, my, bounds[k], bounds[k + 1] - bounds[k],
+                                                               vh0, vc, rec, slot.state, L.norm_w, ctx->d_err);
+    }
+    *n_launch += 2 + 2 * nseg;
     return cudaGetLastError();
 }
 

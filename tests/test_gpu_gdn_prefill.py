@@ -33,8 +33,11 @@ def inputs(seed, T):
             O.normal(seed + 4, (T, 6144)))
 
 
+# T >= 1024 (16 chunks and more) runs the pipelined schedule: chunk segments whose
+# intra-chunk kernels (side stream) overlap the chain kernels of the previous
+# segment; 1000 and 2113 also end on a ragged chunk.
 @pytest.mark.parametrize("T,head0,warm", [(1, 0, False), (3, 2, True), (64, 1, True), (100, 3, True),
-                                          (200, 0, False), (129, 2, True)])
+                                          (200, 0, False), (129, 2, True), (1000, 1, True), (2113, 3, True)])
 def test_gdn_prefill_small(T, head0, warm):
     seed = O.SEED0 + 4000 + T
     ctx, p = make_ctx(seed)
@@ -74,9 +77,9 @@ def test_gdn_prefill_then_decode():
     ctx.close()
 
 
-def test_gdn_prefill_head_slice():
-    seed = O.SEED0 + 4200
-    T = 150
+@pytest.mark.parametrize("T", [150, 1500])
+def test_gdn_prefill_head_slice(T):
+    seed = O.SEED0 + 4200 + T
     a0, a1 = 10, 34
     ctx, p = make_ctx(seed, v_heads=(a0, a1))
     qkv, a, b, z = inputs(seed, T)
