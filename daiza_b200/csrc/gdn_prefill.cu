@@ -68,7 +68,11 @@ __device__ __forceinline__ void store_split4(__nv_bfloat16* hi_row, size_t lo_of
 
 constexpr int PREP_TOK = 4;      // tokens per prep CTA: conv weights and shared input rows are read once for 4 tokens
 
-__global__ void __launch_bounds__(256) gdn_pf_prep_kernel(int64_t T, int64_t Tp, int vh0, int vc, int h0,
+// silu with the fast exponential and division (relative error ~1e-6, far below
+// the bf16 hi/lo operand split that follows)
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+__global__ void __launch_bounds__(256, 4) gdn_pf_prep_kernel(int64_t T, int64_t Tp, int vh0, int vc, int h0,
                                                           const float* __restrict__ qkv,
                                                           const float* __restrict__ hist,
                                                           const float* __restrict__ conv_w,
@@ -124,7 +128,7 @@ __global__ void __launch_bounds__(256) gdn_pf_prep_kernel(int64_t T, int64_t Tp,
                     acc.z = fmaf(xv.z, w[ct].z, acc.z);
                     acc.w = fmaf(xv.w, w[ct].w, acc.w);
                 }
-                acc = make_float4(siluf_acc(acc.x), siluf_acc(acc.y), siluf_acc(acc.z), siluf_acc(acc.w));
+                acc = make_float4(silu_fast(acc.x), silu_fast(acc.y), silu_fast(acc.z), silu_fast(acc.w));
             }
             if (gi < 2 * SSM_HK) {                      // warp-uniform branch: every lane reaches the shuffles
                 const float ss = warp_sum(acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w);
@@ -157,7 +161,9 @@ __global__ void gdn_pf_ring_kernel(int64_t T, int h0, const float* __restrict__ 
 
 template <typename S>
 __device__ __forceinline__ S& align1024(unsigned char* raw) {
-    return *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    // offset the shared-memory pointer itself (integer arithmetic on the address
+    // would turn every later access into a generic one)
+    return *reinterpret_cast<S*>(raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u));
 }
 
 // ---------------------------------------------------------------------------
@@ -244,10 +250,6 @@ __global__ void __launch_bounds__(256, 1) gdn_pf_intra_kernel(const __grid_const
         const int c = i / vc, vl = i % vc, kh = (vh0 + vl) % SSM_HK;
         unsigned char* R = rec + ((size_t)c * vc + vl) * REC_BYTES;
         const uint32_t ph = (uint32_t)(n & 1);
-        if (tid == 0) {
-            bulk_wait_read_all();              // every store of item n-1 (other buffer, P, G) has read smem
-            if (i + (int)gridDim.x < n_items) load_kq(i + gridDim.x, buf ^ 1);
-        }
         wait_or_flag(&sm.bar_kq[buf], (uint32_t)((n >> 1) & 1), err, ok);
         if (!__syncthreads_and(ok)) break;     // every thread takes the same path
         const uint32_t kq_hi = smem_u32(&sm.kq[buf][0][0][0][0]), kq_lo = smem_u32(&sm.kq[buf][1][0][0][0]);
@@ -266,6 +268,11 @@ __global__ void __launch_bounds__(256, 1) gdn_pf_intra_kernel(const __grid_const
                 }
             }
             umma_commit(&sm.bar_m1);
+            // the next item's K/Q go into the other buffer once item n-1's record
+            // store (its W/U0 images live there) has read it; P and G of item n-1
+            // were waited for after its level-1 inverse
+            bulk_wait_read_all();
+            if (i + (int)gridDim.x < n_items) load_kq(i + gridDim.x, buf ^ 1);
         }
         if (warp == 1) {   // inclusive cumsum of the 64 log decays (2 per lane)
             const float a0 = sm.g[buf][2 * lane], a1 = sm.g[buf][2 * lane + 1];
@@ -569,8 +576,6 @@ __device__ __forceinline__ void bfly_reduce(float* a, int lane) {
     }
 }
 
-// silu with the fast exponential and division (relative error ~1e-6)
-__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // U0^T of one record, row v, t in [32h, 32h + 32): eight 16-byte chunks whose
 // positions in the image are XOR-swizzled by v % 8

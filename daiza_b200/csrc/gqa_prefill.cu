@@ -329,7 +329,9 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) pf_attn_kernel(const __grid_c
     using namespace pf;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // dynamic smem is only guaranteed 16-byte aligned: round up to 1 KB
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // offset the shared-memory pointer itself (integer arithmetic on the address
+    // would turn every later access into a generic one)
+    Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nq = GRP * kvc;
     const int n_qt = (int)((T + BM - 1) / BM);
