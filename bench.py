@@ -43,12 +43,12 @@ SEED0 = 0xDA12A000 + 2      # config 2
 HQ, HKV, GRP, HD = 24, 4, 6, 256
 SSM_HV, SSM_D, QKV_LEN, INNER = 48, 128, 10240, 6144
 
-# DRAM bytes that ncu counted for the split-K attention kernel divided by its
-# algorithmic K/V bytes, on the capture summarised in
-# profiles/gqa_split_kernel_config2.md; the roofline's `traffic` is this ratio
-# times the algorithmic bytes of the timed launch (traffic grows with the KV
-# positions read).  None until measured.
-GQA_SPLIT_TRAFFIC_RATIO = None
+# DRAM bytes (read + write) that one ncu capture counted for the split-K
+# attention kernel, divided by the algorithmic bytes of that launch: the first
+# 16 config-2 sequences (205,050 KV positions, 1.681 GB algorithmic, 1.696 GB
+# counted).  Traffic grows with the KV positions read, so the roofline's
+# `traffic` is this ratio times the algorithmic bytes of the timed launch.
+GQA_SPLIT_TRAFFIC_RATIO = 1.0087
 
 
 def seq_lengths():
@@ -303,7 +303,8 @@ def bench_config2(dz, torch, dist, dev, local, rank, world, args):
     """This rank's LPT share of the 64 sequences, timed with CUDA events; the
     headline value uses the max over ranks."""
     from daiza_b200 import parallel as P
-    all_lens = seq_lengths()
+    all_lens = seq_lengths()[:args.sample_seqs] if args.sample_seqs else seq_lengths()
+    n_total = len(all_lens)
     mine = P.lpt_shard(all_lens, world)[rank]
     lens = all_lens[mine]
     B = len(lens)
@@ -403,7 +404,7 @@ def bench_config2(dz, torch, dist, dev, local, rank, world, args):
         ems = _max_over_ranks(dist, dev, e0.elapsed_time(e1))
         h2d = B * (HQ * 2 * HD + 2 * HKV * HD + QKV_LEN + 2 * SSM_HV + INNER) * 4
         d2h = B * (HQ * HD + INNER) * 4
-        e2e = {"value": N_SEQ * args.e2e_steps / (ems / 1000.0), "unit": "tok/s",
+        e2e = {"value": n_total * args.e2e_steps / (ems / 1000.0), "unit": "tok/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "path": "dz_gqa_decode_host + dz_gdn_decode_host (pinned host buffers, copies inside the timed region), "
                        "max over ranks",
@@ -411,11 +412,13 @@ def bench_config2(dz, torch, dist, dev, local, rank, world, args):
     err = ctx.device_error()
     ctx.close()
     traffic = None if GQA_SPLIT_TRAFFIC_RATIO is None else GQA_SPLIT_TRAFFIC_RATIO * gqa_b
-    return {"ms": ms, "ms_rank": ms_rank, "B": B, "kv_tokens": int(lens_at.sum()), "clk": clk, "clocks": clocks,
+    return {"ms": ms, "ms_rank": ms_rank, "B": B, "n_total": n_total, "kv_tokens": int(lens_at.sum()), "clk": clk, "clocks": clocks,
             "launches": launches, "e2e": e2e, "device_error": err,
             "roofline": {"bound": "hbm", "kernel": "dz_gqa_decode (prep + split-K + combine)", "achieved": gqa_gbs,
                          "peak": hbm, "unit": "GB/s", "frac": gqa_gbs / hbm, "traffic": traffic,
                          "peak_kind": f"{peak_kind} hbm_gbs", "bytes_per_launch": gqa_b,
+                         "traffic_source": "ncu dram bytes of gqa_split_kernel on the first 16 config-2 sequences, "
+                                           "scaled by KV positions (ratio %.4f)" % GQA_SPLIT_TRAFFIC_RATIO,
                          "ms_per_launch": float(np.mean(gqa_ms)), "rank": rank},
             "gdn": {"achieved_gbs": gdn_gbs, "frac": gdn_gbs / hbm, "bytes": gdn_b, "ms": float(np.mean(gdn_ms))},
             "step_gbs": (gqa_b + gdn_b) / (ms_rank / args.steps / 1000.0) / 1e9}
@@ -729,18 +732,21 @@ def run_ours(args):
 
     if rank == 0:
         ms = c2["ms"]
-        line = {"metric": METRIC, "value": N_SEQ * args.steps / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+        line = {"metric": METRIC, "value": c2["n_total"] * args.steps / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic",
                 "config": {"workload": "config 2: batched hybrid decode, 64 sequences in total, KV lengths "
                                        "U{512..32768} (seeded), 1 gated GQA + 1 Gated DeltaNet layer, f32 caches",
-                           "sequences": N_SEQ, "seqs_on_rank0": c2["B"], "kv_tokens_on_rank0": c2["kv_tokens"],
+                           "sequences": c2["n_total"], "seqs_on_rank0": c2["B"], "kv_tokens_on_rank0": c2["kv_tokens"],
                            "parallelism": f"sequence-sharded x{world} (LPT on cached length), no collective",
                            "l2": "no flush: per-step KV+state traffic ~9 GB >> 126 MB L2"},
                 "hbm_gbs_step_rank0": c2["step_gbs"], "roofline": c2["roofline"], "gdn": c2["gdn"],
                 "gpu_launches": c2["launches"], "clocks": c2["clk"], "e2e": c2["e2e"], "cpu_baseline": cpu,
                 "device_error": c2["device_error"]}
+        if args.sample_seqs:
+            line["config"]["workload"] = (f"PROFILING SAMPLE, not the benchmark: the first {c2['n_total']} of the 64 "
+                                          "config-2 sequences")
         line.update(extra)
         if c2["clk"] is None and c2["clocks"].raw:
             line["clocks_raw_head"] = c2["clocks"].raw[:300]
@@ -768,6 +774,8 @@ def main():
     ap.add_argument("--stack-steps", type=int, default=10)
     ap.add_argument("--stack-prefill-iters", type=int, default=2)
     ap.add_argument("--prefill-iters", type=int, default=5)
+    ap.add_argument("--sample-seqs", type=int, default=0,
+                    help="profiling only: run config 2 on the first N of its 64 sequences (a few GB instead of ~9)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
