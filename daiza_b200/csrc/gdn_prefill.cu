@@ -27,15 +27,22 @@
 //                 q, k (every k head) and v (local v heads) as bf16 hi/lo rows
 //                 [head][hi|lo][Tp][128] for TMA, log decay g and beta [head][Tp]
 //   gdn_pf_ring   ring-buffer update (after every conv read)
-//   gdn_pf_intra  one CTA per (chunk, v head): [K;Q] K^T, A and P, Tm by
-//                 blocked forward substitution, W^T = K^T (Tm diag(beta e^G))^T
-//                 and U0^T = V^T (Tm diag(beta))^T; writes an 80 KB record
-//                 (W and P as ready-to-use operand images, U0^T, G)
-//   gdn_pf_chain  one persistent CTA per v head: the state lives in TMEM as
-//                 the f32 accumulator [128 v lanes][128 k columns] for the whole
-//                 prefill; per chunk  U^T = U0^T - S W^T,  Y^T = S Qe^T + U^T P^T,
-//                 S = e^{G_last} S + U^T Kd, with warp-specialised loader, MMA
-//                 issuer and epilogues; the gated RMSNorm output is fused.
+//   gdn_pf_intra  persistent CTAs over the (chunk, v head) items: [K;Q] K^T,
+//                 A and P, Tm by blocked forward substitution,
+//                 W^T = K^T (Tm diag(beta e^G))^T and U0^T = V^T (Tm diag(beta))^T;
+//                 writes an 80 KB record per item (W and P as ready-to-use
+//                 operand images, U0^T, G)
+//   gdn_pf_chain  one CTA per v head over a range of chunks: the state lives in
+//                 TMEM as the f32 accumulator [128 v lanes][128 k columns]
+//                 (loaded from and stored back to the SSM state at the ends of
+//                 the range); per chunk  U^T = U0^T - S W^T,
+//                 Y^T = S Qe^T + U^T P^T,  S = e^{G_last} S + U^T Kd, with
+//                 warp-specialised loader, MMA issuer and epilogues; the gated
+//                 RMSNorm output is fused.
+// From 16 chunks on, the chunks are cut into segments: the intra kernel of
+// segment k + 1 runs on a side stream (n_sm - vc CTAs) while the chain kernel of
+// segment k runs on the caller's stream (vc CTAs); events order them, no kernel
+// waits on another.
 #include <algorithm>
 #include <cstddef>
 
