@@ -55,6 +55,15 @@ void free_cache(dz_ctx* ctx) {
     ctx->part_items = 0;
     ctx->n_seqs = 0;
     ctx->caps.clear();
+    for (auto& sn : ctx->snaps) sn.valid = false;
+}
+
+// A KV length of (layer, seq) went down to new_len (truncate, reset, import,
+// fill): snapshots of seq keep the lowest length seen, so a restore can tell
+// whether rows under its saved length may have been rewritten.
+void kv_lowered(dz_ctx* ctx, int layer, int seq, int64_t new_len) {
+    for (auto& sn : ctx->snaps)
+        if (sn.valid && sn.seq == seq && sn.kv_low[layer] > new_len) sn.kv_low[layer] = new_len;
 }
 
 dz_status dev_alloc(dz_ctx* ctx, void** p, size_t bytes, bool zero) {
@@ -232,6 +241,7 @@ dz_status dz_ctx_destroy(dz_ctx* ctx) {
         if (ctx->pf) cudaFree(ctx->pf);
         if (ctx->gdn_rec) cudaFree(ctx->gdn_rec);
         if (ctx->d_err) cudaFree(ctx->d_err);
+        if (ctx->snap_mem) cudaFree(ctx->snap_mem);
         for (auto& e : ctx->pf_ev)
             if (e) cudaEventDestroy(e);
         if (ctx->pf_side) cudaStreamDestroy(ctx->pf_side);
@@ -405,7 +415,10 @@ dz_status dz_kv_truncate(dz_ctx* ctx, int layer, int seq, int64_t new_len) {
     if (!layer_ok(ctx, layer) || !ctx->layers[layer].is_attn || seq < 0 || seq >= ctx->n_seqs || new_len < 0)
         return fail(ctx, DZ_EINVAL, "bad truncate arguments");
     auto& len = ctx->layers[layer].len[seq];
-    if (new_len < len) len = new_len;   // kv_cache.rs:119-129: keep the first new_len tokens
+    if (new_len < len) {
+        len = new_len;   // kv_cache.rs:119-129: keep the first new_len tokens
+        kv_lowered(ctx, layer, seq, new_len);
+    }
     return DZ_OK;
 }
 
@@ -417,6 +430,7 @@ dz_status dz_cache_reset(dz_ctx* ctx, int seq) {
     for (auto& L : ctx->layers) {
         if (L.is_attn) {
             L.len[seq] = 0;
+            kv_lowered(ctx, (int)(&L - ctx->layers.data()), seq, 0);
         } else {
             const size_t per = (size_t)vc * SSM_D * SSM_D + (size_t)CONV_K * QKV_LEN;
             DZ_CUDA(cudaMemset(L.h_ssm[seq].state, 0, per * sizeof(float)));
@@ -463,6 +477,7 @@ dz_status dz_kv_import(dz_ctx* ctx, int layer, int seq, const float* k_flat, con
                              (size_t)kvc * HD * 4, HD * 4, len, cudaMemcpyDefault));
     }
     L.len[seq] = len;
+    kv_lowered(ctx, layer, seq, 0);   // rows rewritten from 0
     return DZ_OK;
 }
 
@@ -509,6 +524,101 @@ dz_status dz_kv_fill_pattern(dz_ctx* ctx, int layer, int seq, int64_t len, int b
         DZ_CUDA(cudaMemset(L.h_kv[seq].v + (size_t)h * L.h_kv[seq].cap * HD, byte_value, (size_t)len * HD * 4));
     }
     L.len[seq] = len;
+    kv_lowered(ctx, layer, seq, 0);   // rows rewritten from 0
+    return DZ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// sequence snapshots
+// ---------------------------------------------------------------------------
+dz_status dz_snapshot_reserve(dz_ctx* ctx, int n_slots) {
+    if (!ctx || n_slots < 0) return fail(ctx, DZ_EINVAL, "n_slots must be >= 0");
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    int n_gdn = 0;
+    for (const auto& L : ctx->layers) n_gdn += L.is_attn ? 0 : 1;
+    const size_t per_layer = (size_t)ctx->cfg.v_head_count * SSM_D * SSM_D + (size_t)CONV_K * QKV_LEN;
+    DZ_CUDA(cudaDeviceSynchronize());   // no copy of an earlier reservation may be in flight
+    if (ctx->snap_mem) cudaFree(ctx->snap_mem);
+    ctx->snap_mem = nullptr;
+    ctx->snaps.clear();
+    ctx->snap_slot_floats = per_layer * n_gdn;
+    if (n_slots == 0) return DZ_OK;
+    cudaError_t e = cudaMalloc(&ctx->snap_mem, std::max<size_t>(ctx->snap_slot_floats, 64) * n_slots * sizeof(float));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        ctx->snap_mem = nullptr;
+        return fail(ctx, DZ_ENOMEM, "snapshot reserve of %d slots (%zu bytes each): %s", n_slots,
+                    ctx->snap_slot_floats * sizeof(float), cudaGetErrorString(e));
+    }
+    ctx->snaps.assign(n_slots, SnapSlot{});
+    return DZ_OK;
+}
+
+static dz_status snapshot_check(dz_ctx* ctx, int seq, int slot) {
+    if (!ctx) return DZ_EINVAL;
+    if (seq < 0 || seq >= ctx->n_seqs) return fail(ctx, DZ_EINVAL, "bad seq %d", seq);
+    if (slot < 0 || slot >= (int)ctx->snaps.size())
+        return fail(ctx, DZ_EINVAL, "snapshot slot %d outside the %d reserved", slot, (int)ctx->snaps.size());
+    return DZ_OK;
+}
+
+dz_status dz_snapshot_save(dz_ctx* ctx, int seq, int slot, void* stream) {
+    dz_status st = snapshot_check(ctx, seq, slot);
+    if (st != DZ_OK) return st;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    const size_t per_layer = (size_t)ctx->cfg.v_head_count * SSM_D * SSM_D + (size_t)CONV_K * QKV_LEN;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    SnapSlot& sn = ctx->snaps[slot];
+    sn.valid = false;
+    const size_t n_layers = ctx->layers.size();
+    sn.kv_len.assign(n_layers, -1);
+    sn.kv_low.assign(n_layers, -1);
+    sn.head.assign(n_layers, 0);
+    float* dst = ctx->snap_mem + (size_t)slot * ctx->snap_slot_floats;
+    for (size_t l = 0; l < n_layers; ++l) {
+        const LayerState& L = ctx->layers[l];
+        if (L.is_attn) {
+            sn.kv_len[l] = sn.kv_low[l] = L.len[seq];
+        } else {
+            // state [vc][128][128] and conv ring [4][10240] are one contiguous block
+            DZ_CUDA(cudaMemcpyAsync(dst, L.h_ssm[seq].state, per_layer * sizeof(float), cudaMemcpyDeviceToDevice, s));
+            sn.head[l] = L.head[seq];
+            dst += per_layer;
+        }
+    }
+    sn.seq = seq;
+    sn.valid = true;
+    return DZ_OK;
+}
+
+dz_status dz_snapshot_restore(dz_ctx* ctx, int seq, int slot, void* stream) {
+    dz_status st = snapshot_check(ctx, seq, slot);
+    if (st != DZ_OK) return st;
+    SnapSlot& sn = ctx->snaps[slot];
+    if (!sn.valid || sn.seq != seq) return fail(ctx, DZ_ESTATE, "snapshot slot %d holds no snapshot of seq %d", slot, seq);
+    for (size_t l = 0; l < ctx->layers.size(); ++l)
+        if (ctx->layers[l].is_attn && sn.kv_low[l] < sn.kv_len[l])
+            return fail(ctx, DZ_ESTATE,
+                        "layer %d of seq %d: KV length went to %lld (below the saved %lld) since the snapshot; "
+                        "the rows it covered may have been rewritten",
+                        (int)l, seq, (long long)sn.kv_low[l], (long long)sn.kv_len[l]);
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    const size_t per_layer = (size_t)ctx->cfg.v_head_count * SSM_D * SSM_D + (size_t)CONV_K * QKV_LEN;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const float* src = ctx->snap_mem + (size_t)slot * ctx->snap_slot_floats;
+    for (size_t l = 0; l < ctx->layers.size(); ++l) {
+        LayerState& L = ctx->layers[l];
+        if (L.is_attn) {
+            L.len[seq] = sn.kv_len[l];   // KvCache::truncate back to the saved length
+        } else {
+            DZ_CUDA(cudaMemcpyAsync(L.h_ssm[seq].state, src, per_layer * sizeof(float), cudaMemcpyDeviceToDevice, s));
+            L.head[seq] = sn.head[l];
+            src += per_layer;
+        }
+    }
     return DZ_OK;
 }
 

@@ -57,6 +57,18 @@ struct LayerState {
 
 }  // namespace dz
 
+namespace dz {
+// one snapshot slot (dz_snapshot_*): per layer the saved KV length and the
+// lowest KV length since the save (-1 for Gated DeltaNet layers), and the conv
+// ring head (Gated DeltaNet layers)
+struct SnapSlot {
+    bool valid = false;
+    int seq = -1;
+    std::vector<int64_t> kv_len, kv_low;
+    std::vector<int> head;
+};
+}  // namespace dz
+
 struct dz_ctx {
     int device = 0;
     int n_sm = 148;
@@ -88,6 +100,10 @@ struct dz_ctx {
     // that order them with the chain kernels (created with the context)
     cudaStream_t pf_side = nullptr;
     cudaEvent_t pf_ev[dz::PF_MAX_SEGMENTS + 1] = {};
+    // sequence snapshots: slots of snap_slot_floats floats each (sized by the config)
+    float* snap_mem = nullptr;
+    size_t snap_slot_floats = 0;
+    std::vector<dz::SnapSlot> snaps;
 };
 
 namespace dz {

@@ -128,6 +128,19 @@ class Context:
     def cache_reset(self, seq):
         self._chk(self.lib.dz_cache_reset(self.h, seq))
 
+    # ---- sequence snapshots (speculative rollback) ------------------------
+    def snapshot_reserve(self, n_slots):
+        """Device memory for n_slots snapshots of one sequence's recurrent state."""
+        self._chk(self.lib.dz_snapshot_reserve(self.h, int(n_slots)))
+
+    def snapshot_save(self, seq, slot, stream=None):
+        """DeltaNet states, conv rings and heads of every layer plus the KV lengths."""
+        self._chk(self.lib.dz_snapshot_save(self.h, int(seq), int(slot), _stream(stream)))
+
+    def snapshot_restore(self, seq, slot, stream=None):
+        """Back to the saved state; KV lengths truncated to the saved ones."""
+        self._chk(self.lib.dz_snapshot_restore(self.h, int(seq), int(slot), _stream(stream)))
+
     def kv_export(self, layer, seq):
         n = self.kv_len(layer, seq)
         k = np.zeros((n, self.kvc, HD), np.float32)

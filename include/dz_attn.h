@@ -168,6 +168,30 @@ dz_status dz_gqa_prefill_at(dz_ctx* ctx, int layer, int seq, int64_t start_pos, 
 dz_status dz_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* qkv, const float* alpha,
                          const float* beta, const float* z, float* y, void* stream);
 
+/* ---- sequence snapshots (speculative rollback) --------------------------- */
+/* A snapshot holds one sequence's recurrent state across every layer: for each
+ * Gated DeltaNet layer the state [v heads][128][128], the conv ring [4][10240]
+ * and its head; for each full-attention layer the KV length (the KV rows
+ * themselves stay in the cache: restoring is KvCache::truncate back to that
+ * length, kv_cache.rs:119-129).  This is the SSM state snapshot/restore that
+ * lets a drafter's k tokens be verified as one batched prefill and rolled back
+ * on rejection -- the step the reference leaves out and verifies token by
+ * token instead (Daiza-runtime/src/engine.rs:1295-1305).
+ *
+ * dz_snapshot_reserve allocates n_slots slots of device memory (each holds
+ * Gated-DeltaNet-layers x (v heads x 16384 + 40960) floats) and drops earlier
+ * slots.  dz_snapshot_save copies the sequence's state into a slot;
+ * dz_snapshot_restore copies it back and sets every KV length to the saved
+ * one; a slot can be restored any number of times.  Both copies are
+ * stream-ordered device-to-device copies on `stream`.  Restore fails with
+ * DZ_ESTATE if the slot holds no snapshot of this sequence, or if some KV
+ * length went below the saved one since the save (cache reset, truncate,
+ * import or fill: the rows under the saved length may have been rewritten).
+ * dz_cache_create empties every slot. */
+dz_status dz_snapshot_reserve(dz_ctx* ctx, int n_slots);
+dz_status dz_snapshot_save(dz_ctx* ctx, int seq, int slot, void* stream);
+dz_status dz_snapshot_restore(dz_ctx* ctx, int seq, int slot, void* stream);
+
 /* ---- host-buffer convenience (end-to-end path) -------------------------- */
 /* Same as dz_gqa_decode / dz_gdn_decode with HOST input/output pointers and
  * HOST seq_ids; copies in, computes, copies out on `stream`, then waits. */
