@@ -20,6 +20,8 @@ Extra keys on the same line:
   stack              config 4: the 64-layer stack head-sharded over the ranks
                      with an NCCL all-gather per layer (decode B = 8 at context
                      131072, prefill T = 32768); every N
+  q1_gemv            the Q1_0 input-projection GEMV that feeds the cores (hidden
+                     5120, 1 and 4 tokens); N = 1 only
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -532,6 +534,71 @@ def bench_single_layer(dz, torch, dev, local, kind, reps=20):
             "issue": note, "device_error": err}
 
 
+Q1_SETS = (("attention input projections attn_q/attn_k/attn_v (model/attention.rs:80-87)", (12288, 1024, 1024)),
+           ("Gated DeltaNet input projections attn_qkv/ssm_alpha/ssm_beta/attn_gate (model/ssm.rs:451-463)",
+            (10240, 48, 48, 6144)))
+Q1_HIDDEN = 5120
+
+
+def bench_q1(dz, torch, local, tokens=(1, 4)):
+    """Q1_0 projection GEMV (dz_q1_gemv) on the model's two input-projection
+    sets from hidden 5120, for a few tokens: 24 calls over 24 distinct copies of
+    the weights (10-12 MB each, ~250 MB in all > L2) captured in one CUDA graph
+    and replayed.  Synthetic Q1_0 weights (random signs, |N(0,0.02)| binary16
+    scales); roofline bytes = the Q1_0 bytes + x + y."""
+    import oracle as O
+    dev = torch.device("cuda", local)
+    ctx = dz.Context(local, dz.default_config(n_layers=2, full_attention_interval=2))
+    hbm, _, kind = peaks()
+    out = []
+    for name, rows in Q1_SETS:
+        base = [O.q1_random(SEED0 + 900 + i, r, Q1_HIDDEN) for i, r in enumerate(rows)]
+        copies = [[torch.from_numpy(w).to(dev) for w in base] for _ in range(24)]
+        wbytes = sum(w.nbytes for w in base)
+        for T in tokens:
+            x = torch.randn(T, Q1_HIDDEN, device=dev)
+            ys = [torch.empty(T, r, device=dev) for r in rows]
+            for _ in range(3):
+                ctx.q1_gemv(copies[0], x, ys)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(24):
+                    ctx.q1_gemv(copies[i], x, ys)
+            for _ in range(2):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1000.0 / 240
+            nbytes = wbytes + T * Q1_HIDDEN * 4 + T * sum(rows) * 4
+            out.append({"set": name, "rows": sum(rows), "cols": Q1_HIDDEN, "tokens": T, "us": us,
+                        "weight_mb": wbytes / 1e6, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / hbm,
+                        "peak_kind": f"{kind} hbm_gbs"})
+            del graph
+        del copies
+    # CPU baseline: the oracle's restatement of the reference matvec, all host cores, first set, 1 token
+    cores = os.cpu_count() or 1
+    base = [O.q1_random(SEED0 + 900 + i, r, Q1_HIDDEN) for i, r in enumerate(Q1_SETS[0][1])]
+    xh = O.normal(SEED0 + 950, (1, Q1_HIDDEN))
+    O.q1_gemv(base, xh, n_threads=cores)
+    t0 = time.perf_counter()
+    reps = 5
+    for _ in range(reps):
+        O.q1_gemv(base, xh, n_threads=cores)
+    cpu_us = (time.perf_counter() - t0) / reps * 1e6
+    err = ctx.device_error()
+    ctx.close()
+    return {"workload": "Q1_0 projection GEMV (dz_q1_gemv), hidden 5120, synthetic weights",
+            "runs": out, "device_error": err,
+            "cpu_baseline": {"us": cpu_us, "cores": cores, "kind": "port",
+                             "sample": "attention input projection set, 1 token, dot_q1_0_row over all rows"}}
+
+
 PF_T = 8192
 
 
@@ -720,6 +787,8 @@ def run_ours(args):
         extra["config1"] = bench_single_layer(dz, torch, dev, local, "gdn")
     if world == 1 and not args.no_prefill:
         extra["prefill"] = bench_prefill(dz, torch, local, args)
+    if world == 1 and not args.no_q1:
+        extra["q1_gemv"] = bench_q1(dz, torch, local)
     if not args.no_stack:
         torch.cuda.empty_cache()
         extra["stack"] = bench_stack(dz, torch, dist, dev, local, rank, world, args)
@@ -769,6 +838,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-single", action="store_true", help="skip the config 0 / config 1 single-layer keys")
     ap.add_argument("--no-stack", action="store_true", help="skip the config 4 stack key")
+    ap.add_argument("--no-q1", action="store_true", help="skip the Q1_0 projection GEMV key")
     ap.add_argument("--stack-ctx", type=int, default=131072)
     ap.add_argument("--stack-prefill", type=int, default=32768)
     ap.add_argument("--stack-steps", type=int, default=10)

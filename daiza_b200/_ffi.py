@@ -54,6 +54,7 @@ SIGNATURES = {
     "dz_kv_fill_pattern": [_P, _I, _I, _I64, _I],
     "dz_gqa_decode": [_P, _I, _I, _P, _P, _P, _P, _P, _P],
     "dz_gqa_decode_at": [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P],
+    "dz_q1_gemv": [_P, _I, _P, _P, _I, _I, _P, _P, _P],
     "dz_snapshot_reserve": [_P, _I],
     "dz_snapshot_save": [_P, _I, _I, _P],
     "dz_snapshot_restore": [_P, _I, _I, _P],

@@ -155,6 +155,15 @@ cudaError_t ensure_prefill_scratch(dz_ctx* ctx, size_t bytes) {
     if (e == cudaSuccess) ctx->pf_bytes = bytes;
     return e;
 }
+cudaError_t ensure_q1_scratch(dz_ctx* ctx, size_t bytes) {
+    if (ctx->q1_bytes >= bytes) return cudaSuccess;
+    if (ctx->q1) cudaFree(ctx->q1);
+    ctx->q1 = nullptr;
+    ctx->q1_bytes = 0;
+    cudaError_t e = cudaMalloc(&ctx->q1, bytes);
+    if (e == cudaSuccess) ctx->q1_bytes = bytes;
+    return e;
+}
 cudaError_t ensure_decode_records(dz_ctx* ctx, size_t bytes) {
     if (ctx->gdn_rec_bytes >= bytes) return cudaSuccess;
     if (ctx->gdn_rec) cudaFree(ctx->gdn_rec);
@@ -240,6 +249,7 @@ dz_status dz_ctx_destroy(dz_ctx* ctx) {
         if (ctx->stage) cudaFree(ctx->stage);
         if (ctx->pf) cudaFree(ctx->pf);
         if (ctx->gdn_rec) cudaFree(ctx->gdn_rec);
+        if (ctx->q1) cudaFree(ctx->q1);
         if (ctx->d_err) cudaFree(ctx->d_err);
         if (ctx->snap_mem) cudaFree(ctx->snap_mem);
         for (auto& e : ctx->pf_ev)
@@ -525,6 +535,42 @@ dz_status dz_kv_fill_pattern(dz_ctx* ctx, int layer, int seq, int64_t len, int b
     }
     L.len[seq] = len;
     kv_lowered(ctx, layer, seq, 0);   // rows rewritten from 0
+    return DZ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Q1_0 projection GEMV
+// ---------------------------------------------------------------------------
+dz_status dz_q1_gemv(dz_ctx* ctx, int n_mats, const void* const* w, const int32_t* rows, int cols, int T,
+                     const float* x, float* const* y, void* stream) {
+    if (!ctx) return DZ_EINVAL;
+    if (n_mats < 1 || n_mats > Q1_MAX_MATS)
+        return fail(ctx, DZ_EINVAL, "n_mats=%d outside 1..%d", n_mats, Q1_MAX_MATS);
+    if (T < 1 || T > Q1_MAX_T) return fail(ctx, DZ_EINVAL, "T=%d outside 1..%d tokens", T, Q1_MAX_T);
+    if (cols <= 0 || cols % 1024 != 0) return fail(ctx, DZ_EINVAL, "cols=%d is not a positive multiple of 1024", cols);
+    if (!w || !rows || !x || !y) return fail(ctx, DZ_EINVAL, "null argument");
+    if (reinterpret_cast<uintptr_t>(x) % 16 != 0) return fail(ctx, DZ_EINVAL, "x must be 16-byte aligned");
+    int64_t blocks = 0;
+    for (int m = 0; m < n_mats; ++m) {
+        if (!w[m] || !y[m] || rows[m] <= 0) return fail(ctx, DZ_EINVAL, "matrix %d: null pointer or rows <= 0", m);
+        if (reinterpret_cast<uintptr_t>(w[m]) % 16 != 0)
+            return fail(ctx, DZ_EINVAL, "matrix %d: weights must be 16-byte aligned", m);
+        blocks += (rows[m] + 63) / 64;
+    }
+    if (blocks >= ((int64_t)1 << 31)) return fail(ctx, DZ_EINVAL, "too many rows");
+    const size_t smem = q1_smem_bytes(cols, T);
+    int max_smem = 0;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    DZ_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
+    if (smem > (size_t)max_smem)
+        return fail(ctx, DZ_EINVAL, "cols=%d with T=%d needs %zu bytes of shared memory per CTA (limit %d)", cols, T,
+                    smem, max_smem);
+    int launches = 0;
+    cudaError_t e = launch_q1_gemv(ctx, n_mats, reinterpret_cast<const uint8_t* const*>(w), rows, cols, T, x, y,
+                                   static_cast<cudaStream_t>(stream), &launches);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "q1 gemv launch");
+    ctx->last_launches = launches;
     return DZ_OK;
 }
 

@@ -12,6 +12,8 @@ namespace dz {
 constexpr int MAXB = 256;   // sequences per kernel launch (descriptor rides in the kernel parameters)
 constexpr int MAXC = 256;   // max split-K chunks per (sequence, kv head) in decode
 constexpr int PF_MAX_SEGMENTS = 16;   // chunk segments of a pipelined Gated DeltaNet prefill
+constexpr int Q1_MAX_MATS = 8;        // matrices sharing one input in a Q1_0 GEMV launch
+constexpr int Q1_MAX_T = 8;           // tokens (input rows) of a Q1_0 GEMV launch
 
 // One sequence's KV cache for one full-attention layer:
 //   k, v: [kv_head_count][cap][256] f32 -- per kv head a contiguous [seq, dim]
@@ -96,6 +98,9 @@ struct dz_ctx {
     // Gated DeltaNet decode records of the two-kernel decode path (grown on demand)
     float* gdn_rec = nullptr;
     size_t gdn_rec_bytes = 0;
+    // Q1_0 GEMV: the prepared input (fixed-point digit planes, slice sums, scales), grown on demand
+    void* q1 = nullptr;
+    size_t q1_bytes = 0;
     // Gated DeltaNet prefill: side stream of the intra-chunk kernels and the events
     // that order them with the chain kernels (created with the context)
     cudaStream_t pf_side = nullptr;
@@ -172,6 +177,12 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
                                const float* beta, const float* z, float* y, cudaStream_t st, int* n_launch);
 // grows ctx->pf to at least `bytes`
 cudaError_t ensure_prefill_scratch(dz_ctx* ctx, size_t bytes);
+// Q1_0 projection GEMV (q1_gemv.cu): dynamic shared memory of one CTA, and the launch
+size_t q1_smem_bytes(int cols, int T);
+cudaError_t launch_q1_gemv(dz_ctx* ctx, int n_mats, const uint8_t* const* w, const int32_t* rows, int cols, int T,
+                           const float* x, float* const* y, cudaStream_t st, int* n_launch);
+// grows ctx->q1 to at least `bytes`
+cudaError_t ensure_q1_scratch(dz_ctx* ctx, size_t bytes);
 // grows ctx->gdn_rec to at least `bytes`
 cudaError_t ensure_decode_records(dz_ctx* ctx, size_t bytes);
 }  // namespace dz

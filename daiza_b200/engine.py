@@ -128,6 +128,19 @@ class Context:
     def cache_reset(self, seq):
         self._chk(self.lib.dz_cache_reset(self.h, seq))
 
+    # ---- Q1_0 projection GEMV ---------------------------------------------
+    def q1_gemv(self, ws, x, ys, stream=None):
+        """Q1_0Matrix::matvec_multi_into_slice for x [T][cols] (T <= 8) and up to
+        8 Q1_0 matrices ws (uint8 device tensors [rows][cols/128*18]); writes
+        ys[m] [T][rows]."""
+        rows = np.array([w.shape[0] for w in ws], np.int32)
+        cols = x.shape[-1]
+        T = x.shape[0] if x.dim() == 2 else 1
+        wp = (C.c_void_p * len(ws))(*[w.data_ptr() for w in ws])
+        yp = (C.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
+        self._chk(self.lib.dz_q1_gemv(self.h, len(ws), C.cast(wp, C.c_void_p), _np_ptr(rows), cols, T, _ptr(x),
+                                      C.cast(yp, C.c_void_p), _stream(stream)))
+
     # ---- sequence snapshots (speculative rollback) ------------------------
     def snapshot_reserve(self, n_slots):
         """Device memory for n_slots snapshots of one sequence's recurrent state."""

@@ -168,6 +168,27 @@ dz_status dz_gqa_prefill_at(dz_ctx* ctx, int layer, int seq, int64_t start_pos, 
 dz_status dz_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const float* qkv, const float* alpha,
                          const float* beta, const float* z, float* y, void* stream);
 
+/* ---- Q1_0 projection GEMV ------------------------------------------------- */
+/* The projections that feed the cores: Q1_0Matrix::matvec_multi_into_slice
+ * (Daiza-engine/src/model/weights.rs:831; row kernel tensor/quant.rs:267-328),
+ * for T <= 8 tokens (the multi-token verify path) and up to 8 matrices that
+ * share the input, e.g. attn_q / attn_k / attn_v (model/attention.rs:80-87) or
+ * attn_qkv / ssm_alpha / ssm_beta / attn_gate (model/ssm.rs:451-463).
+ *   w[m]    device pointer to matrix m in the reference's Q1_0 bytes: rows[m]
+ *           rows of cols/128 blocks of 18 bytes (binary16 scale, little endian,
+ *           then 16 sign bytes; bit b of byte j is weight 8j+b, 1 -> +scale,
+ *           0 -> -scale); 16-byte aligned
+ *   x       device [T][cols] f32, 16-byte aligned
+ *   y[m]    device [T][rows[m]] f32
+ * cols must be a multiple of 1024 (every projection of the model is) and small
+ * enough for one CTA's shared memory: 64 rows of weights plus ~3*T*cols bytes of
+ * prepared input (cols 5120 or 6144: any T <= 8; cols 17408: T = 1).  The input
+ * is quantised to 23-bit fixed point per 128-input group (context-owned
+ * scratch, grown on first use) and the integer dots are exact: outputs agree
+ * with f32 arithmetic to ~1e-6 of the output scale. */
+dz_status dz_q1_gemv(dz_ctx* ctx, int n_mats, const void* const* w, const int32_t* rows, int cols, int T,
+                     const float* x, float* const* y, void* stream);
+
 /* ---- sequence snapshots (speculative rollback) --------------------------- */
 /* A snapshot holds one sequence's recurrent state across every layer: for each
  * Gated DeltaNet layer the state [v heads][128][128], the conv ring [4][10240]

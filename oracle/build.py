@@ -2,7 +2,7 @@
 
 Compiles ``dz_oracle.cpp`` into ``oracle/libdzoracle.so`` with the flags that
 make it follow the Rust reference bit for bit on the same CPU:
-``-mavx2 -mfma`` (same intrinsics) and ``-ffp-contract=off`` (rustc never fuses
+``-mavx2 -mfma -mf16c`` (same intrinsics) and ``-ffp-contract=off`` (rustc never fuses
 a separate multiply and add).
 
 The reference itself (Rust, Cargo workspace) cannot be compiled here: there is
@@ -21,7 +21,7 @@ def build(force: bool = False) -> str:
     if (not force and os.path.exists(OUT)
             and os.path.getmtime(OUT) >= os.path.getmtime(SRC)):
         return OUT
-    cmd = ["g++", "-O2", "-std=c++17", "-mavx2", "-mfma", "-ffp-contract=off",
+    cmd = ["g++", "-O2", "-std=c++17", "-mavx2", "-mfma", "-mf16c", "-ffp-contract=off",
            "-fno-fast-math", "-fPIC", "-shared", "-pthread", SRC, "-o", OUT + ".tmp"]
     subprocess.check_call(cmd)
     os.replace(OUT + ".tmp", OUT)

@@ -728,6 +728,85 @@ extern "C" int oc_gdn_decode_batch(int B, const float* qkv, const float* alpha, 
 }
 
 // ---------------------------------------------------------------------------
+// Q1_0 projection GEMV -- tensor/quant.rs, model/weights.rs
+// ---------------------------------------------------------------------------
+// Q1_0 layout (tensor/dtype.rs:11-14, README "Q1_0 quantization format"): each
+// row is cols/128 blocks of 18 bytes -- the group scale as IEEE binary16
+// (little endian), then 16 sign bytes; bit b of sign byte j is weight 8j+b of
+// the group, 1 -> +scale, 0 -> -scale.
+
+// SIGN_LUT (quant.rs:212-225): byte -> 8 lanes of +-1.0
+struct alignas(32) SignLutEntry { float v[8]; };
+static const SignLutEntry* sign_lut() {
+    static SignLutEntry lut[256];
+    static bool init = false;
+    if (!init) {
+        for (int idx = 0; idx < 256; ++idx)
+            for (int bit = 0; bit < 8; ++bit) lut[idx].v[bit] = ((idx >> bit) & 1) ? 1.0f : -1.0f;
+        init = true;
+    }
+    return lut;
+}
+
+// dot_q1_0_row_avx2 (quant.rs:267-328): per group four 8-lane accumulators of
+// LUT(byte) * x, group_acc = (acc0 + acc1) + (acc2 + acc3), then
+// acc = fma(scale, group_acc, acc); one horizontal sum at the end.  The scale is
+// converted by _mm256_cvtph_ps (exact, subnormals included).
+static float dot_q1_0_row(const uint8_t* data, int64_t row, int cols, const float* x, const SignLutEntry* lut) {
+    const int groups = cols / 128;
+    const uint8_t* rowp = data + row * (int64_t)groups * 18;
+    __m256 acc_vec = _mm256_setzero_ps();
+    for (int g = 0; g < groups; ++g) {
+        const uint8_t* blk = rowp + (size_t)g * 18;
+        const uint16_t scale_bits = (uint16_t)(blk[0] | (blk[1] << 8));
+        const __m256 scale_v = _mm256_cvtph_ps(_mm_set1_epi16((short)scale_bits));
+        const uint8_t* sp = blk + 2;
+        const float* xp = x + (size_t)g * 128;
+        __m256 a0 = _mm256_setzero_ps(), a1 = _mm256_setzero_ps(), a2 = _mm256_setzero_ps(),
+               a3 = _mm256_setzero_ps();
+        for (int bi = 0; bi < 16; bi += 4) {
+            a0 = _mm256_fmadd_ps(_mm256_load_ps(lut[sp[bi]].v), _mm256_loadu_ps(xp + bi * 8), a0);
+            a1 = _mm256_fmadd_ps(_mm256_load_ps(lut[sp[bi + 1]].v), _mm256_loadu_ps(xp + (bi + 1) * 8), a1);
+            a2 = _mm256_fmadd_ps(_mm256_load_ps(lut[sp[bi + 2]].v), _mm256_loadu_ps(xp + (bi + 2) * 8), a2);
+            a3 = _mm256_fmadd_ps(_mm256_load_ps(lut[sp[bi + 3]].v), _mm256_loadu_ps(xp + (bi + 3) * 8), a3);
+        }
+        const __m256 group_acc = _mm256_add_ps(_mm256_add_ps(a0, a1), _mm256_add_ps(a2, a3));
+        acc_vec = _mm256_fmadd_ps(scale_v, group_acc, acc_vec);
+    }
+    return hsum_ps(acc_vec);
+}
+
+// matvec_multi_into_slice (weights.rs:831-...) for T tokens: every matrix row of
+// every token through dot_q1_0_row, rows split over n_threads workers.
+// y[m] is [T][rows[m]].
+extern "C" void oc_q1_gemv(int n_mats, const uint8_t* const* w, const int32_t* rows, int cols, int T,
+                           const float* x, float* const* y, int n_threads) {
+    const SignLutEntry* lut = sign_lut();
+    int64_t total = 0;
+    for (int m = 0; m < n_mats; ++m) total += rows[m];
+    auto work = [&](int64_t r0, int64_t r1) {
+        for (int64_t gr = r0; gr < r1; ++gr) {
+            int m = 0;
+            int64_t r = gr;
+            while (r >= rows[m]) r -= rows[m++];
+            for (int t = 0; t < T; ++t)
+                y[m][(int64_t)t * rows[m] + r] = dot_q1_0_row(w[m], r, cols, x + (size_t)t * cols, lut);
+        }
+    };
+    if (n_threads <= 1) {
+        work(0, total);
+        return;
+    }
+    std::vector<std::thread> th;
+    const int64_t per = (total + n_threads - 1) / n_threads;
+    for (int i = 0; i < n_threads; ++i) {
+        const int64_t a = i * per, b = std::min(total, a + per);
+        if (a < b) th.emplace_back(work, a, b);
+    }
+    for (auto& t : th) t.join();
+}
+
+// ---------------------------------------------------------------------------
 // Portable seeded generator shared by tests and the bench's CPU leg:
 // splitmix64 -> uniform doubles in (0,1) -> Box-Muller (double) -> f32.
 // ---------------------------------------------------------------------------

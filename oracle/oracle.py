@@ -65,6 +65,8 @@ def lib():
                                           _f32p, C.c_int]
         L.oc_gdn_decode_batch.argtypes = [C.c_int, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
                                           C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), _i32p, _f32p, C.c_int]
+        L.oc_q1_gemv.argtypes = [C.c_int, C.POINTER(C.c_void_p), _i32p, C.c_int, C.c_int, _f32p,
+                                 C.POINTER(C.c_void_p), C.c_int]
         L.oc_fill_normal.argtypes = [C.c_uint64, _f32p, C.c_int64, C.c_float, C.c_float]
         L.oc_fill_uniform.argtypes = [C.c_uint64, _f32p, C.c_int64, C.c_float, C.c_float]
         L.oc_fill_uniform_int.argtypes = [C.c_uint64, _i64p, C.c_int64, C.c_int64, C.c_int64]
@@ -360,3 +362,48 @@ def gdn_decode_inputs(seed):
     hist[1:] = normal(seed + 15, (CONV_K - 1, QKV_LEN))   # head=0: slot 0 is the oldest (overwritten)
     state = normal(seed + 16, (SSM_HV, SSM_D, SSM_D), 0.0, 0.02)
     return qkv, alpha, beta, z, hist, state
+
+
+# ---------------------------------------------------------------------------
+# Q1_0 projection GEMV (tensor/quant.rs:267-328, model/weights.rs:831)
+# ---------------------------------------------------------------------------
+Q1_GROUP, Q1_BLOCK = 128, 18
+
+
+def q1_random(seed, rows, cols, scale_std=0.02):
+    """A seeded Q1_0 matrix: rows x cols/128 blocks of 18 bytes (binary16 scale,
+    little endian, then 16 sign bytes).  Scales are |N(0, scale_std)| as
+    binary16, signs uniform."""
+    assert cols % Q1_GROUP == 0
+    g = cols // Q1_GROUP
+    scales = np.abs(normal(seed, (rows, g), 0.0, scale_std)).astype(np.float16)
+    u = uniform(seed + 1, (rows, g, 16), 0.0, 256.0)
+    signs = np.minimum(u, 255.0).astype(np.uint8)
+    blk = np.empty((rows, g, Q1_BLOCK), np.uint8)
+    blk[:, :, 0:2] = scales.view(np.uint8).reshape(rows, g, 2)
+    blk[:, :, 2:] = signs
+    return blk.reshape(rows, g * Q1_BLOCK)
+
+
+def q1_dequant(w, cols):
+    """f32 weights of a Q1_0 matrix (tests only)."""
+    rows = w.shape[0]
+    g = cols // Q1_GROUP
+    blk = w.reshape(rows, g, Q1_BLOCK)
+    scales = blk[:, :, 0:2].copy().view(np.float16).astype(np.float32).reshape(rows, g, 1)
+    bits = np.unpackbits(blk[:, :, 2:], axis=2, bitorder="little").astype(np.float32)
+    return ((2.0 * bits - 1.0) * scales).reshape(rows, cols)
+
+
+def q1_gemv(ws, x, n_threads=1):
+    """matvec_multi_into_slice for T tokens: ws is a list of Q1_0 matrices
+    ([rows][cols/128*18] uint8) sharing x [T][cols]; returns [T][rows] per matrix."""
+    x = _c(np.atleast_2d(x))
+    T, cols = x.shape
+    ws = [np.ascontiguousarray(w, np.uint8) for w in ws]
+    rows = np.array([w.shape[0] for w in ws], np.int32)
+    ys = [np.empty((T, r), np.float32) for r in rows]
+    wp = (C.c_void_p * len(ws))(*[w.ctypes.data for w in ws])
+    yp = (C.c_void_p * len(ys))(*[y.ctypes.data for y in ys])
+    lib().oc_q1_gemv(len(ws), wp, rows, cols, T, x.reshape(-1), yp, n_threads)
+    return ys

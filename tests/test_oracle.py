@@ -176,3 +176,18 @@ def test_golden_fixtures_match_oracle(oracle):
         for key in want.files:
             # exact on this host; a tiny slack covers _mm256_rcp_ps differing by CPU vendor
             assert rel_err(got[key], want[key]) <= 1e-6, f"{name}:{key} drifted"
+
+
+def test_q1_gemv_oracle_matches_float64_dequant(oracle):
+    """dot_q1_0_row restated (LUT FMA, per-group scale) against the float64
+    product of the dequantised matrix; multi-matrix split and token layout."""
+    O = oracle
+    w = O.q1_random(O.SEED0 + 61, 96, 1024)
+    w2 = O.q1_random(O.SEED0 + 62, 17, 1024)
+    x = O.normal(O.SEED0 + 63, (3, 1024))
+    y, y2 = O.q1_gemv([w, w2], x, n_threads=3)
+    for yy, ww in ((y, w), (y2, w2)):
+        ref = x.astype(np.float64) @ O.q1_dequant(ww, 1024).T.astype(np.float64)
+        assert yy.shape == ref.shape
+        assert np.abs(yy - ref).max() <= 1e-6 * np.abs(ref).max()
+    assert np.array_equal(O.q1_gemv([w], x[1:2])[0][0], y[1])
