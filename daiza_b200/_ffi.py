@@ -9,9 +9,9 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdzattn.so")
 
-DZ_OK, DZ_EINVAL, DZ_ENOMEM, DZ_ECUDA, DZ_ENCCL, DZ_ETIMEOUT, DZ_ESTATE = range(7)
+DZ_OK, DZ_EINVAL, DZ_ENOMEM, DZ_ECUDA, DZ_ENCCL, DZ_ETIMEOUT, DZ_ESTATE, DZ_EIO = range(8)
 STATUS_NAMES = {0: "DZ_OK", 1: "DZ_EINVAL", 2: "DZ_ENOMEM", 3: "DZ_ECUDA", 4: "DZ_ENCCL",
-                5: "DZ_ETIMEOUT", 6: "DZ_ESTATE"}
+                5: "DZ_ETIMEOUT", 6: "DZ_ESTATE", 7: "DZ_EIO"}
 
 
 class DzError(RuntimeError):
@@ -55,6 +55,8 @@ SIGNATURES = {
     "dz_gqa_decode": [_P, _I, _I, _P, _P, _P, _P, _P, _P],
     "dz_gqa_decode_at": [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P],
     "dz_q1_gemv": [_P, _I, _P, _P, _I, _I, _P, _P, _P],
+    "dz_session_save": [_P, _I, C.c_char_p, _I64, _P, _I64, _I, C.c_char_p],
+    "dz_session_load": [_P, _I, C.c_char_p, _P, _P, _I64, _P, _P, _P, _I64, _P],
     "dz_snapshot_reserve": [_P, _I],
     "dz_snapshot_save": [_P, _I, _I, _P],
     "dz_snapshot_restore": [_P, _I, _I, _P],

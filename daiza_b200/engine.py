@@ -16,6 +16,7 @@ Device tensors are torch CUDA tensors (torch is used for device memory and
 streams only); every computation runs in libdzattn.so.
 """
 import ctypes as C
+import os
 
 import numpy as np
 
@@ -140,6 +141,28 @@ class Context:
         yp = (C.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
         self._chk(self.lib.dz_q1_gemv(self.h, len(ws), C.cast(wp, C.c_void_p), _np_ptr(rows), cols, T, _ptr(x),
                                       C.cast(yp, C.c_void_p), _stream(stream)))
+
+    # ---- DZSS session files ------------------------------------------------
+    def session_save(self, seq, path, pos, history=(), think_enabled=False, system_prompt=None):
+        """Session::save_to_disk (Daiza-runtime/src/session_persist.rs:76-140) for one sequence."""
+        h = np.ascontiguousarray(np.asarray(history, np.uint32))
+        sp = None if system_prompt is None else system_prompt.encode("utf-8")
+        self._chk(self.lib.dz_session_save(self.h, int(seq), os.fspath(path).encode(), int(pos),
+                                           _np_ptr(h) if h.size else None, int(h.size), int(bool(think_enabled)),
+                                           sp))
+
+    def session_load(self, seq, path, history_cap=1 << 20, prompt_cap=1 << 20):
+        """Session::load_from_disk (session_persist.rs:186-290) into sequence seq;
+        returns pos, history tokens, think flag and system prompt (or None)."""
+        pos, n_hist, think, plen = C.c_int64(), C.c_int64(), C.c_int(), C.c_int64()
+        hist = np.zeros(max(1, history_cap), np.uint32)
+        buf = C.create_string_buffer(max(1, prompt_cap))
+        self._chk(self.lib.dz_session_load(self.h, int(seq), os.fspath(path).encode(), C.byref(pos), _np_ptr(hist),
+                                           int(history_cap), C.byref(n_hist), C.byref(think), buf, int(prompt_cap),
+                                           C.byref(plen)))
+        prompt = None if plen.value < 0 else buf.raw[:plen.value].decode("utf-8", "replace")
+        return {"pos": pos.value, "history": hist[:n_hist.value].copy(), "think_enabled": bool(think.value),
+                "system_prompt": prompt}
 
     # ---- sequence snapshots (speculative rollback) ------------------------
     def snapshot_reserve(self, n_slots):

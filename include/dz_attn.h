@@ -37,7 +37,8 @@ typedef enum {
     DZ_ECUDA = 3,     /* a CUDA runtime call failed */
     DZ_ENCCL = 4,     /* reserved for collective failures */
     DZ_ETIMEOUT = 5,  /* a bounded wait ran out */
-    DZ_ESTATE = 6     /* call order violated (e.g. no cache yet, cache full) */
+    DZ_ESTATE = 6,    /* call order violated (e.g. no cache yet, cache full) */
+    DZ_EIO = 7        /* session file could not be written, read or parsed */
 } dz_status;
 
 typedef struct dz_ctx dz_ctx;
@@ -212,6 +213,33 @@ dz_status dz_q1_gemv(dz_ctx* ctx, int n_mats, const void* const* w, const int32_
 dz_status dz_snapshot_reserve(dz_ctx* ctx, int n_slots);
 dz_status dz_snapshot_save(dz_ctx* ctx, int seq, int slot, void* stream);
 dz_status dz_snapshot_restore(dz_ctx* ctx, int seq, int slot, void* stream);
+
+/* ---- DZSS session files -------------------------------------------------- */
+/* Save / restore one sequence's caches in the reference's session format v1
+ * (Daiza-runtime/src/session_persist.rs:1-36, save_to_disk :76-140,
+ * load_from_disk :186-290): a 128-byte header ("DZSS", version 1, cfg_hash,
+ * pos, n_history, n_blocks, think flag, system-prompt flag), the history
+ * tokens, then per layer either the KV cache (kind 0: per_token, len, K and V
+ * as f32 [len][kv head][256]) or the DeltaNet state (kind 1: state, conv
+ * history, conv_head), then the optional system prompt.  The files are byte
+ * compatible with the reference's, provided the model matches: cfg_hash is
+ * Rust's DefaultHasher (SipHash-1-3, zero key) over the reference's ten
+ * config fields, with hidden = 5120 and context_length = 262144 (Bonsai-27B).
+ * Only contexts that own whole layers (no head slice) read or write sessions.
+ *
+ * dz_session_save writes the file; pos, the history tokens, think_enabled and
+ * system_prompt (NUL-terminated, or NULL) are the session fields the library
+ * does not hold.  dz_session_load checks magic, version, cfg_hash, block count,
+ * layer kinds and sizes, reads every block, then imports them into `seq`
+ * (KV lengths must fit the caches' capacities: DZ_ESTATE otherwise).
+ * *n_history gets the file's token count (DZ_EINVAL if it exceeds
+ * history_cap); *prompt_len the prompt's byte count or -1 when there is none
+ * (the buffer needs prompt_len + 1 bytes).  Format and I/O errors: DZ_EIO. */
+dz_status dz_session_save(dz_ctx* ctx, int seq, const char* path, int64_t pos, const uint32_t* history,
+                          int64_t n_history, int think_enabled, const char* system_prompt);
+dz_status dz_session_load(dz_ctx* ctx, int seq, const char* path, int64_t* pos, uint32_t* history,
+                          int64_t history_cap, int64_t* n_history, int* think_enabled, char* system_prompt,
+                          int64_t prompt_cap, int64_t* prompt_len);
 
 /* ---- host-buffer convenience (end-to-end path) -------------------------- */
 /* Same as dz_gqa_decode / dz_gdn_decode with HOST input/output pointers and
