@@ -21,7 +21,8 @@ Extra keys on the same line:
                      with an NCCL all-gather per layer (decode B = 8 at context
                      131072, prefill T = 32768); every N
   q1_gemv            the Q1_0 input-projection GEMV that feeds the cores (hidden
-                     5120, 1 and 4 tokens); N = 1 only
+                     5120, 1 and 4 tokens) and the block tail after them
+                     (post-norm + SwiGLU MLP, d_ff 17408); N = 1 only
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -538,13 +539,16 @@ Q1_SETS = (("attention input projections attn_q/attn_k/attn_v (model/attention.r
            ("Gated DeltaNet input projections attn_qkv/ssm_alpha/ssm_beta/attn_gate (model/ssm.rs:451-463)",
             (10240, 48, 48, 6144)))
 Q1_HIDDEN = 5120
+Q1_FF = 17408
 
 
 def bench_q1(dz, torch, local, tokens=(1, 4)):
     """Q1_0 projection GEMV (dz_q1_gemv) on the model's two input-projection
     sets from hidden 5120, for a few tokens: 24 calls over 24 distinct copies of
     the weights (10-12 MB each, ~250 MB in all > L2) captured in one CUDA graph
-    and replayed.  Synthetic Q1_0 weights (random signs, |N(0,0.02)| binary16
+    and replayed.  Then the block tail (dz_block_mlp: RMSNorm, gate/up GEMV,
+    SwiGLU, down GEMV added into h) over 12 copies of one block's MLP weights
+    (d_ff 17408, 37.6 MB each); its roofline bytes are the Q1_0 bytes.  Synthetic Q1_0 weights (random signs, |N(0,0.02)| binary16
     scales); roofline bytes = the Q1_0 bytes + x + y."""
     import oracle as O
     dev = torch.device("cuda", local)
@@ -581,6 +585,36 @@ def bench_q1(dz, torch, local, tokens=(1, 4)):
                         "peak_kind": f"{kind} hbm_gbs"})
             del graph
         del copies
+    # block tail (dz_block_mlp): post-norm + SwiGLU MLP of one block, 12 distinct weight copies (~450 MB)
+    mlp_w = [O.q1_random(SEED0 + 960, Q1_FF, Q1_HIDDEN), O.q1_random(SEED0 + 961, Q1_FF, Q1_HIDDEN),
+             O.q1_random(SEED0 + 962, Q1_HIDDEN, Q1_FF, 0.01)]
+    mcopies = [[torch.from_numpy(w).to(dev) for w in mlp_w] for _ in range(12)]
+    post = torch.ones(Q1_HIDDEN, device=dev)
+    mbytes = sum(w.nbytes for w in mlp_w)
+    for T in tokens:
+        h = torch.randn(T, Q1_HIDDEN, device=dev)
+        for _ in range(3):
+            ctx.block_mlp(h, post, *mcopies[0])
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(12):
+                ctx.block_mlp(h, post, *mcopies[i])
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / 120
+        out.append({"set": "block_mlp", "rows": 2 * Q1_FF + Q1_HIDDEN, "cols": f"{Q1_HIDDEN}/{Q1_FF}", "tokens": T,
+                    "us": us, "weight_mb": mbytes / 1e6, "gbs": mbytes / us / 1e3, "frac": mbytes / us / 1e3 / hbm,
+                    "peak_kind": f"{kind} hbm_gbs"})
+        del graph
+    del mcopies
     # CPU baseline: the oracle's restatement of the reference matvec, all host cores, first set, 1 token
     cores = os.cpu_count() or 1
     base = [O.q1_random(SEED0 + 900 + i, r, Q1_HIDDEN) for i, r in enumerate(Q1_SETS[0][1])]

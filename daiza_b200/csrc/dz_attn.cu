@@ -250,6 +250,7 @@ dz_status dz_ctx_destroy(dz_ctx* ctx) {
         if (ctx->pf) cudaFree(ctx->pf);
         if (ctx->gdn_rec) cudaFree(ctx->gdn_rec);
         if (ctx->q1) cudaFree(ctx->q1);
+        if (ctx->mlp) cudaFree(ctx->mlp);
         if (ctx->d_err) cudaFree(ctx->d_err);
         if (ctx->snap_mem) cudaFree(ctx->snap_mem);
         for (auto& e : ctx->pf_ev)
@@ -541,9 +542,9 @@ dz_status dz_kv_fill_pattern(dz_ctx* ctx, int layer, int seq, int64_t len, int b
 // ---------------------------------------------------------------------------
 // Q1_0 projection GEMV
 // ---------------------------------------------------------------------------
-dz_status dz_q1_gemv(dz_ctx* ctx, int n_mats, const void* const* w, const int32_t* rows, int cols, int T,
-                     const float* x, float* const* y, void* stream) {
-    if (!ctx) return DZ_EINVAL;
+// checks of one Q1_0 GEMV launch and the launch itself (device already current)
+static dz_status q1_gemv_impl(dz_ctx* ctx, int n_mats, const void* const* w, const int32_t* rows, int cols, int T,
+                              const float* x, float* const* y, bool accumulate, cudaStream_t st, int* launches) {
     if (n_mats < 1 || n_mats > Q1_MAX_MATS)
         return fail(ctx, DZ_EINVAL, "n_mats=%d outside 1..%d", n_mats, Q1_MAX_MATS);
     if (T < 1 || T > Q1_MAX_T) return fail(ctx, DZ_EINVAL, "T=%d outside 1..%d tokens", T, Q1_MAX_T);
@@ -560,16 +561,90 @@ dz_status dz_q1_gemv(dz_ctx* ctx, int n_mats, const void* const* w, const int32_
     if (blocks >= ((int64_t)1 << 31)) return fail(ctx, DZ_EINVAL, "too many rows");
     const size_t smem = q1_smem_bytes(cols, T);
     int max_smem = 0;
-    DeviceGuard g(ctx->device);
-    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
     DZ_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
     if (smem > (size_t)max_smem)
         return fail(ctx, DZ_EINVAL, "cols=%d with T=%d needs %zu bytes of shared memory per CTA (limit %d)", cols, T,
                     smem, max_smem);
-    int launches = 0;
     cudaError_t e = launch_q1_gemv(ctx, n_mats, reinterpret_cast<const uint8_t* const*>(w), rows, cols, T, x, y,
-                                   static_cast<cudaStream_t>(stream), &launches);
+                                   accumulate, st, launches);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "q1 gemv launch");
+    return DZ_OK;
+}
+
+dz_status dz_q1_gemv(dz_ctx* ctx, int n_mats, const void* const* w, const int32_t* rows, int cols, int T,
+                     const float* x, float* const* y, void* stream) {
+    if (!ctx) return DZ_EINVAL;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    int launches = 0;
+    dz_status st = q1_gemv_impl(ctx, n_mats, w, rows, cols, T, x, y, false, static_cast<cudaStream_t>(stream),
+                                &launches);
+    if (st == DZ_OK) ctx->last_launches = launches;
+    return st;
+}
+
+dz_status dz_q1_gemv_add(dz_ctx* ctx, int n_mats, const void* const* w, const int32_t* rows, int cols, int T,
+                         const float* x, float* const* y, void* stream) {
+    if (!ctx) return DZ_EINVAL;
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    int launches = 0;
+    dz_status st = q1_gemv_impl(ctx, n_mats, w, rows, cols, T, x, y, true, static_cast<cudaStream_t>(stream),
+                                &launches);
+    if (st == DZ_OK) ctx->last_launches = launches;
+    return st;
+}
+
+// ---------------------------------------------------------------------------
+// block MLP (block.rs:93-124 + mlp.rs:28-58)
+// ---------------------------------------------------------------------------
+dz_status dz_block_mlp(dz_ctx* ctx, int T, int hidden, int d_ff, float* h, const float* post_norm_w,
+                       const void* w_gate, const void* w_up, const void* w_down, void* stream) {
+    if (!ctx) return DZ_EINVAL;
+    if (T < 1 || T > Q1_MAX_T) return fail(ctx, DZ_EINVAL, "T=%d outside 1..%d tokens", T, Q1_MAX_T);
+    if (hidden <= 0 || hidden % 1024 != 0 || d_ff <= 0 || d_ff % 1024 != 0)
+        return fail(ctx, DZ_EINVAL, "hidden=%d and d_ff=%d must be positive multiples of 1024", hidden, d_ff);
+    if (!h || !post_norm_w || !w_gate || !w_up || !w_down) return fail(ctx, DZ_EINVAL, "null argument");
+    if (reinterpret_cast<uintptr_t>(h) % 16 != 0) return fail(ctx, DZ_EINVAL, "h must be 16-byte aligned");
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    const size_t need = ((size_t)T * hidden + (size_t)2 * T * d_ff) * sizeof(float);
+    if (ctx->mlp_bytes < need) {
+        if (ctx->mlp) cudaFree(ctx->mlp);
+        ctx->mlp = nullptr;
+        ctx->mlp_bytes = 0;
+        DZ_CUDA(cudaMalloc(&ctx->mlp, need));
+        ctx->mlp_bytes = need;
+    }
+    float* normed = ctx->mlp;
+    float* gate = normed + (size_t)T * hidden;
+    float* up = gate + (size_t)T * d_ff;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int launches = 0;
+    // post_attention_norm (block.rs:93-104)
+    cudaError_t e = launch_rmsnorm_rows(h, post_norm_w, ctx->cfg.rms_eps, T, hidden, normed, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "rmsnorm launch");
+    ++launches;
+    // gate and up share the normed input (mlp.rs:43-46)
+    const void* gu[2] = {w_gate, w_up};
+    const int32_t gu_rows[2] = {d_ff, d_ff};
+    float* gu_out[2] = {gate, up};
+    dz_status st = q1_gemv_impl(ctx, 2, gu, gu_rows, hidden, T, normed, gu_out, false, s, &launches);
+    if (st != DZ_OK) return st;
+    // silu(gate) * up (mlp.rs:48)
+    if ((e = launch_swiglu(gate, up, (int64_t)T * d_ff, s)) != cudaSuccess) return cuda_fail(ctx, e, "swiglu launch");
+    ++launches;
+    // h += W_down (silu(gate) * up) (mlp.rs:50), one token per launch at the widest inputs
+    int per = T;
+    while (per > 1 && (size_t)q1_smem_bytes(d_ff, per) > (size_t)227 * 1024) per /= 2;
+    const int32_t down_rows[1] = {hidden};
+    for (int t0 = 0; t0 < T; t0 += per) {
+        const int n = std::min(per, T - t0);
+        const void* wd[1] = {w_down};
+        float* yo[1] = {h + (size_t)t0 * hidden};
+        st = q1_gemv_impl(ctx, 1, wd, down_rows, d_ff, n, gate + (size_t)t0 * d_ff, yo, true, s, &launches);
+        if (st != DZ_OK) return st;
+    }
     ctx->last_launches = launches;
     return DZ_OK;
 }

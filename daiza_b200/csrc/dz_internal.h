@@ -101,6 +101,9 @@ struct dz_ctx {
     // Q1_0 GEMV: the prepared input (fixed-point digit planes, slice sums, scales), grown on demand
     void* q1 = nullptr;
     size_t q1_bytes = 0;
+    // block MLP: normed rows, gate and up activations, grown on demand
+    float* mlp = nullptr;
+    size_t mlp_bytes = 0;
     // Gated DeltaNet prefill: side stream of the intra-chunk kernels and the events
     // that order them with the chain kernels (created with the context)
     cudaStream_t pf_side = nullptr;
@@ -180,7 +183,10 @@ cudaError_t ensure_prefill_scratch(dz_ctx* ctx, size_t bytes);
 // Q1_0 projection GEMV (q1_gemv.cu): dynamic shared memory of one CTA, and the launch
 size_t q1_smem_bytes(int cols, int T);
 cudaError_t launch_q1_gemv(dz_ctx* ctx, int n_mats, const uint8_t* const* w, const int32_t* rows, int cols, int T,
-                           const float* x, float* const* y, cudaStream_t st, int* n_launch);
+                           const float* x, float* const* y, bool accumulate, cudaStream_t st, int* n_launch);
+// block tail (block_tail.cu): RMSNorm rows and SwiGLU, stream-ordered
+cudaError_t launch_rmsnorm_rows(const float* x, const float* w, float eps, int T, int n, float* out, cudaStream_t st);
+cudaError_t launch_swiglu(float* gate, const float* up, int64_t n, cudaStream_t st);
 // grows ctx->q1 to at least `bytes`
 cudaError_t ensure_q1_scratch(dz_ctx* ctx, size_t bytes);
 // grows ctx->gdn_rec to at least `bytes`

@@ -51,6 +51,7 @@ constexpr int PLANES = 3;
 
 struct Q1Desc {
     int n_mats, cols, T;
+    int accumulate;              // y += W x (matvec_add_into_slice) instead of y = W x
     const uint8_t* w[Q1_MAX_MATS];
     float* y[Q1_MAX_MATS];
     int rows[Q1_MAX_MATS];
@@ -240,13 +241,14 @@ __global__ void __launch_bounds__(q1::THREADS, TT <= 2 ? 2 : 1) q1_gemv_kernel(Q
             float v = part[(size_t)r * T + t];
 #pragma unroll
             for (int k = 1; k < KSPLIT; ++k) v += part[((size_t)k * ROWS + r) * T + t];
-            d.y[m][(size_t)t * rows + r0 + r] = v;
+            float* yp = d.y[m] + (size_t)t * rows + r0 + r;
+            *yp = d.accumulate ? *yp + v : v;
         }
     }
 }
 
 cudaError_t launch_q1_gemv(dz_ctx* ctx, int n_mats, const uint8_t* const* w, const int32_t* rows, int cols, int T,
-                           const float* x, float* const* y, cudaStream_t st, int* n_launch) {
+                           const float* x, float* const* y, bool accumulate, cudaStream_t st, int* n_launch) {
     cudaError_t e = ensure_q1_scratch(ctx, q1_prep_bytes(cols, T));
     if (e != cudaSuccess) return e;
     unsigned char* prep = static_cast<unsigned char*>(ctx->q1);
@@ -254,6 +256,7 @@ cudaError_t launch_q1_gemv(dz_ctx* ctx, int n_mats, const uint8_t* const* w, con
     d.n_mats = n_mats;
     d.cols = cols;
     d.T = T;
+    d.accumulate = accumulate ? 1 : 0;
     d.blk0[0] = 0;
     for (int m = 0; m < n_mats; ++m) {
         d.w[m] = w[m];

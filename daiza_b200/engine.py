@@ -142,6 +142,23 @@ class Context:
         self._chk(self.lib.dz_q1_gemv(self.h, len(ws), C.cast(wp, C.c_void_p), _np_ptr(rows), cols, T, _ptr(x),
                                       C.cast(yp, C.c_void_p), _stream(stream)))
 
+    def q1_gemv_add(self, ws, x, ys, stream=None):
+        """matvec_add_into_slice: ys[m] += ws[m] x (same arguments as q1_gemv)."""
+        rows = np.array([w.shape[0] for w in ws], np.int32)
+        cols = x.shape[-1]
+        T = x.shape[0] if x.dim() == 2 else 1
+        wp = (C.c_void_p * len(ws))(*[w.data_ptr() for w in ws])
+        yp = (C.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
+        self._chk(self.lib.dz_q1_gemv_add(self.h, len(ws), C.cast(wp, C.c_void_p), _np_ptr(rows), cols, T, _ptr(x),
+                                          C.cast(yp, C.c_void_p), _stream(stream)))
+
+    def block_mlp(self, h, post_norm_w, w_gate, w_up, w_down, stream=None):
+        """block.rs:93-124 + mlp.rs:28-51 on h [T][hidden] in place."""
+        T, hidden = h.shape
+        d_ff = w_gate.shape[0]
+        self._chk(self.lib.dz_block_mlp(self.h, T, hidden, d_ff, _ptr(h), _ptr(post_norm_w), _ptr(w_gate),
+                                        _ptr(w_up), _ptr(w_down), _stream(stream)))
+
     # ---- DZSS session files ------------------------------------------------
     def session_save(self, seq, path, pos, history=(), think_enabled=False, system_prompt=None):
         """Session::save_to_disk (Daiza-runtime/src/session_persist.rs:76-140) for one sequence."""

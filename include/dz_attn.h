@@ -214,6 +214,27 @@ dz_status dz_snapshot_reserve(dz_ctx* ctx, int n_slots);
 dz_status dz_snapshot_save(dz_ctx* ctx, int seq, int slot, void* stream);
 dz_status dz_snapshot_restore(dz_ctx* ctx, int seq, int slot, void* stream);
 
+/* Q1_0Matrix::matvec_add_into_slice (model/weights.rs:334-...): the same GEMV
+ * with y[m][t][r] += instead of =, as the output projections accumulate into
+ * the residual stream (attention.rs:207 attn_output, ssm.rs:615 ssm_out). */
+dz_status dz_q1_gemv_add(dz_ctx* ctx, int n_mats, const void* const* w, const int32_t* rows, int cols, int T,
+                         const float* x, float* const* y, void* stream);
+
+/* ---- block tail: post-norm + SwiGLU MLP ------------------------------------ */
+/* The rest of a block after the attention / Gated DeltaNet output projection
+ * (model/block.rs:93-124 with mlp.rs:28-51), for T <= 8 tokens:
+ *   normed = rmsnorm(h, post_norm_w, eps)                (rmsnorm_into)
+ *   gate, up = W_gate normed, W_up normed                (one two-matrix GEMV)
+ *   h += W_down (silu(gate) * up)                        (matvec_add_into_slice)
+ * h: device [T][hidden] f32, updated in place (16-byte aligned); post_norm_w:
+ * device [hidden] f32; W_gate, W_up: Q1_0 [d_ff][hidden]; W_down: Q1_0
+ * [hidden][d_ff] (device, 16-byte aligned; Bonsai-27B: hidden 5120, d_ff
+ * 17408).  Intermediate rows live in context-owned scratch (grown on first
+ * use).  With the output projection done by dz_q1_gemv_add, a whole block runs
+ * on the device between the input projections and the next block. */
+dz_status dz_block_mlp(dz_ctx* ctx, int T, int hidden, int d_ff, float* h, const float* post_norm_w,
+                       const void* w_gate, const void* w_up, const void* w_down, void* stream);
+
 /* ---- DZSS session files -------------------------------------------------- */
 /* Save / restore one sequence's caches in the reference's session format v1
  * (Daiza-runtime/src/session_persist.rs:1-36, save_to_disk :76-140,

@@ -407,3 +407,28 @@ def q1_gemv(ws, x, n_threads=1):
     yp = (C.c_void_p * len(ys))(*[y.ctypes.data for y in ys])
     lib().oc_q1_gemv(len(ws), wp, rows, cols, T, x.reshape(-1), yp, n_threads)
     return ys
+
+
+def rmsnorm_into(src, w, eps):
+    """math/rmsnorm.rs:85-140 (rmsnorm_into_avx2) per row: (x * inv_rms) * w with
+    inv_rms = 1 / sqrt(sum x^2 / n + eps), in f32."""
+    src = _c(np.atleast_2d(src))
+    ss = np.einsum("ij,ij->i", src.astype(np.float64), src.astype(np.float64)).astype(np.float32)
+    inv = (np.float32(1.0) / np.sqrt(ss / np.float32(src.shape[1]) + np.float32(eps))).astype(np.float32)
+    return ((src * inv[:, None]) * _c(w)[None, :]).astype(np.float32)
+
+
+def swiglu(gate, up):
+    """math/simd_exp.rs:273-296 scalar form: silu(gate) * up = gate / (1 + exp(-gate)) * up."""
+    g = _c(gate)
+    return ((g / (np.float32(1.0) + np.exp(-g))) * _c(up)).astype(np.float32)
+
+
+def block_mlp(h, post_norm_w, w_gate, w_up, w_down, eps, n_threads=16):
+    """model/block.rs:93-124 with mlp.rs:28-51 for T tokens (h [T][hidden]):
+    h + W_down (silu(W_gate n) * (W_up n)), n = rmsnorm(h).  Returns the new h."""
+    h = _c(np.atleast_2d(h))
+    normed = rmsnorm_into(h, post_norm_w, eps)
+    gate, up = q1_gemv([w_gate, w_up], normed, n_threads)
+    act = swiglu(gate, up)
+    return (h + q1_gemv([w_down], act, n_threads)[0]).astype(np.float32)
