@@ -250,6 +250,7 @@ dz_status dz_ctx_destroy(dz_ctx* ctx) {
         if (ctx->pf) cudaFree(ctx->pf);
         if (ctx->gdn_rec) cudaFree(ctx->gdn_rec);
         if (ctx->q1) cudaFree(ctx->q1);
+        free_q1_maps(ctx);
         if (ctx->mlp) cudaFree(ctx->mlp);
         if (ctx->d_err) cudaFree(ctx->d_err);
         if (ctx->snap_mem) cudaFree(ctx->snap_mem);
@@ -548,7 +549,8 @@ static dz_status q1_gemv_impl(dz_ctx* ctx, int n_mats, const void* const* w, con
     if (n_mats < 1 || n_mats > Q1_MAX_MATS)
         return fail(ctx, DZ_EINVAL, "n_mats=%d outside 1..%d", n_mats, Q1_MAX_MATS);
     if (T < 1 || T > Q1_MAX_T) return fail(ctx, DZ_EINVAL, "T=%d outside 1..%d tokens", T, Q1_MAX_T);
-    if (cols <= 0 || cols % 1024 != 0) return fail(ctx, DZ_EINVAL, "cols=%d is not a positive multiple of 1024", cols);
+    if (cols <= 0 || cols % 1024 != 0 || cols > 65536)
+        return fail(ctx, DZ_EINVAL, "cols=%d is not a multiple of 1024 in 1024..65536", cols);
     if (!w || !rows || !x || !y) return fail(ctx, DZ_EINVAL, "null argument");
     if (reinterpret_cast<uintptr_t>(x) % 16 != 0) return fail(ctx, DZ_EINVAL, "x must be 16-byte aligned");
     int64_t blocks = 0;
@@ -556,9 +558,11 @@ static dz_status q1_gemv_impl(dz_ctx* ctx, int n_mats, const void* const* w, con
         if (!w[m] || !y[m] || rows[m] <= 0) return fail(ctx, DZ_EINVAL, "matrix %d: null pointer or rows <= 0", m);
         if (reinterpret_cast<uintptr_t>(w[m]) % 16 != 0)
             return fail(ctx, DZ_EINVAL, "matrix %d: weights must be 16-byte aligned", m);
-        blocks += (rows[m] + 63) / 64;
+        blocks += (rows[m] + 127) / 128;
     }
-    if (blocks >= ((int64_t)1 << 31)) return fail(ctx, DZ_EINVAL, "too many rows");
+    if (blocks > q1_max_blocks())
+        return fail(ctx, DZ_EINVAL, "%lld blocks of 128 rows exceed the limit of %d per call", (long long)blocks,
+                    q1_max_blocks());
     const size_t smem = q1_smem_bytes(cols, T);
     int max_smem = 0;
     DZ_CUDA(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
@@ -634,7 +638,7 @@ dz_status dz_block_mlp(dz_ctx* ctx, int T, int hidden, int d_ff, float* h, const
     // silu(gate) * up (mlp.rs:48)
     if ((e = launch_swiglu(gate, up, (int64_t)T * d_ff, s)) != cudaSuccess) return cuda_fail(ctx, e, "swiglu launch");
     ++launches;
-    // h += W_down (silu(gate) * up) (mlp.rs:50), one token per launch at the widest inputs
+    // h += W_down (silu(gate) * up) (mlp.rs:50)
     int per = T;
     while (per > 1 && (size_t)q1_smem_bytes(d_ff, per) > (size_t)227 * 1024) per /= 2;
     const int32_t down_rows[1] = {hidden};

@@ -101,6 +101,7 @@ struct dz_ctx {
     // Q1_0 GEMV: the prepared input (fixed-point digit planes, slice sums, scales), grown on demand
     void* q1 = nullptr;
     size_t q1_bytes = 0;
+    void* q1_maps = nullptr;     // tensor maps of recently used Q1_0 matrices (q1_gemv.cu)
     // block MLP: normed rows, gate and up activations, grown on demand
     float* mlp = nullptr;
     size_t mlp_bytes = 0;
@@ -182,6 +183,8 @@ cudaError_t launch_gdn_prefill(dz_ctx* ctx, int layer, int seq, int64_t T, const
 cudaError_t ensure_prefill_scratch(dz_ctx* ctx, size_t bytes);
 // Q1_0 projection GEMV (q1_gemv.cu): dynamic shared memory of one CTA, and the launch
 size_t q1_smem_bytes(int cols, int T);
+int q1_max_blocks();
+void free_q1_maps(dz_ctx* ctx);
 cudaError_t launch_q1_gemv(dz_ctx* ctx, int n_mats, const uint8_t* const* w, const int32_t* rows, int cols, int T,
                            const float* x, float* const* y, bool accumulate, cudaStream_t st, int* n_launch);
 // block tail (block_tail.cu): RMSNorm rows and SwiGLU, stream-ordered

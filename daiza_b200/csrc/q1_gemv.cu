@@ -1,108 +1,104 @@
-// q1_gemv.cu -- Q1_0 projection GEMV for a few tokens.
+// q1_gemv.cu -- Q1_0 projection GEMV for a few tokens on the tcgen05 integer
+// tensor cores.
 //
 // Reference: Daiza-engine/src/model/weights.rs:831 (matvec_multi_into_slice: up
-// to 8 Q1_0 matrices sharing one input row) with the row kernel
-// tensor/quant.rs:267-328 (dot_q1_0_row_avx2) and its multi-token twin
-// (weights.rs verify4t path).  Q1_0 row layout: cols/128 blocks of 18 bytes --
-// the group scale as IEEE binary16 (little endian), then 16 sign bytes whose bit
-// b of byte j is weight 8j + b (1 -> +scale, 0 -> -scale).
+// to 8 Q1_0 matrices sharing one input row), weights.rs:334
+// (matvec_add_into_slice: y += W x) with the row kernel tensor/quant.rs:267-328
+// (dot_q1_0_row_avx2) and its multi-token twin (weights.rs verify4t path).
+// Q1_0 row layout: cols/128 blocks of 18 bytes -- the group scale as IEEE
+// binary16 (little endian), then 16 sign bytes whose bit b of byte j is weight
+// 8j + b (1 -> +scale, 0 -> -scale).
 //
 // With s_i = +-1 the signs of a group, sum_i s_i x_i = 2 sum_{bit_i = 1} x_i - sum_i x_i,
 // and both sums are exact in integers once x is in fixed point:
 //   1. q1_prep (one warp per (token, group of 128 inputs)): x ~= s_tg q with
-//      |q| <= QMAX and s_tg = max|x over the group| / QMAX; q is stored as
-//      three signed int8 digit planes (q = 65536 d2 + 256 d1 + d0) and, per
-//      16-element slice, the sum of q (the "- sum x" term), in context-owned
-//      scratch.
-//   2. q1_gemv (one CTA of 16 warps per 64-row block of one matrix, a
-//      programmatic dependent of 1): thread 0 starts the bulk copy of the
-//      block's Q1_0 rows at once and the copy of the prepared input after the
-//      grid-dependency wait.  Warp w takes rows 16 (w % 4) .. +15 over a quarter
-//      of the groups (w / 4); a lane owns a 16-weight slice of each of its
-//      groups for 4 rows, so each input slice it loads serves 4 rows: the
-//      slice's 16 sign bits become four words of 0/1 bytes (one multiply and
-//      one mask per 4 weights), __dp4a against the three digit planes gives the
-//      integer sum over the set bits, 2 A - S the exact slice dot, and the
-//      group scale (binary16 -> f32, exact) times s_tg weighs it into an f32
-//      accumulator; shuffles sum the 8 slices of a row, shared memory the 4
-//      quarters.
+//      |q| <= QMAX and s_tg = max|x over the group| / QMAX; q = 65536 d2 +
+//      256 d1 + d0 with signed 8-bit digits.  Column n = 3t + p of the MMA's
+//      B operand is digit plane p of token t (NB blocks of 8 columns, unused
+//      columns zero); prep writes the B fragments of mma.m16n8k32 in register
+//      order, per group and K step, plus per column the factor 2 * 256^p * s_tg
+//      and (plane 0 only) the term s_tg * sum q.
+//   2. q1_gemv (persistent, a programmatic dependent of 1): the work is a list
+//      of items (128-row block, 8 groups), cut into equal contiguous ranges,
+//      one per CTA.  A loader thread brings each item's 128 x 144 weight bytes
+//      (one 2-D TMA box of the Q1_0 rows) and its 8 groups of B fragments into
+//      a two-slot ring.  Warp w of 8 takes rows 16w .. 16w+15: per group, lane
+//      (g, q) reads sign word q of rows g and g+8 and turns it into A fragments
+//      with (word >> s) & 0x01010101 -- bits s, s+8, s+16, s+24 as 0/1 bytes --
+//      so K step s of the group uses bits s and s+4 of every word, and the B
+//      fragments follow the same order.  mma.sync.m16n8k32 (s8 x s8 -> s32)
+//      sums the set bits' digits exactly over the group; each int32 column
+//      value then enters an f32 sum per (row, column) as
+//      scale * (factor * a - term).  When a block is complete the 3 plane
+//      columns of each token are added into y.  A row block split between
+//      CTAs is summed in a fixed order by the CTA that finishes it last
+//      (partials in scratch, a counter per block that the reducing CTA
+//      resets), so results do not depend on timing.
+// Why mma.sync: a tcgen05.mma with M = 128 occupies the tensor core for about
+// 200 cycles at any N from 16 to 256, so with N = 3T <= 24 it would process
+// 128 x 32 weights per 200 cycles -- a tenth of the HBM rate.  The register-
+// operand m16n8k32 runs at about 0.4 per cycle per SM (512 weights each) and
+// needs no shared-memory staging of the expanded signs.
 // The only rounding beyond f32 accumulation is the input quantisation (~1e-7 of
 // the group's max|x| per element).  Roofline: HBM -- the Q1_0 bytes (1.125 bits
-// per weight) are read once -- but the integer work per weight and token
-// (4 ops to expand 4 signs, 12 dp4a per 16 weights) sets the pace.
+// per weight) are read once.
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cstddef>
 
 #include "dz_internal.h"
+#include "tc_common.cuh"
 
 namespace dz {
 
 namespace q1 {
-constexpr int ROWS = 64;         // rows per CTA: 4 row quads of 16 rows
-constexpr int KSPLIT = 4;        // group quarters per row quad (one warp each)
-constexpr int THREADS = 32 * 4 * KSPLIT;
-constexpr int RL = 4;            // rows per lane: 4 row sets x 8 slices per warp, 4 rows per set
-constexpr int PREP_WARPS = 8;    // groups per prep CTA
-constexpr int QMAX = 8355000;    // |q| bound: three signed 8-bit digits reach +-8,355,711
+constexpr int ROWS = 128;                    // rows per item
+constexpr int UNIT = 8;                      // groups per item
+constexpr int UNIT_BYTES = UNIT * 18;        // 144 bytes of each row per item
+constexpr int WBYTES = ROWS * UNIT_BYTES;    // 18432: one item's weights
+constexpr int NS = 2;                        // item slots in shared memory
+constexpr int CWARPS = 8;                    // compute warps (16 rows each)
+constexpr int THREADS = 32 * (CWARPS + 1);   // + one loader warp
+constexpr int CTAS_PER_SM = 2;
+constexpr int QMAX = 8355000;                // |q| bound: three signed 8-bit digits reach +-8,355,711
 constexpr int PLANES = 3;
+constexpr int PREP_WARPS = 8;
+constexpr int MAX_BLOCKS = 4096;             // row blocks per call
 }  // namespace q1
 
+// column blocks of 8 (3T columns) and the prepared bytes of one group:
+// B fragments [NB][32 lanes][4 K steps][2 words], then per block and lane quad q the
+// column pair's (factor, factor, term, term) as f32 [NB][4][4]
+__host__ __device__ inline int q1_nb(int T) { return (3 * T + 7) / 8; }
+__host__ __device__ inline int q1_group_bytes(int T) { return q1_nb(T) * (4 * 256 + 64); }
+
+constexpr int Q1_MAX_KS = 4;                 // CTAs per cluster: 1, 2 or 4
+
+size_t q1_smem_bytes(int cols, int T) {
+    (void)cols;
+    const size_t slot = (size_t)q1::WBYTES + (size_t)q1::UNIT * q1_group_bytes(T);
+    return 128 + q1::NS * slot + (size_t)q1::ROWS * 25 * 4 + (size_t)Q1_MAX_KS * q1::ROWS * T * 4 + 64;
+}
+int q1_max_blocks() { return q1::MAX_BLOCKS; }
+
 struct Q1Desc {
-    int n_mats, cols, T;
-    int accumulate;              // y += W x (matvec_add_into_slice) instead of y = W x
-    const uint8_t* w[Q1_MAX_MATS];
+    CUtensorMap map[Q1_MAX_MATS];   // the Q1_0 rows of each matrix as a [rows][rowbytes] byte tensor
     float* y[Q1_MAX_MATS];
     int rows[Q1_MAX_MATS];
-    int blk0[Q1_MAX_MATS + 1];   // first CTA of each matrix
+    int blk0[Q1_MAX_MATS + 1];      // first 128-row block of each matrix
+    int n_mats, cols, T, accumulate;
+    int units;                      // items per row block (groups / 8)
+    int ks;                         // CTAs per cluster sharing each row block's units
 };
 
-// prepared input (scratch, copied whole into each CTA's shared memory): digit planes
-// [3][T][cols] int8 | slice sums [T][groups][8] int32 | group scales [T][groups] f32
-// (padded to 16 bytes)
-__host__ __device__ inline size_t q1_prep_bytes(int cols, int T) {
-    const size_t groups = (size_t)cols / 128;
-    return (size_t)q1::PLANES * T * cols + (size_t)T * groups * 8 * 4 + ((size_t)T * groups * 4 + 15) / 16 * 16;
-}
-size_t q1_smem_bytes(int cols, int T) {
-    return (size_t)q1::ROWS * (cols / 128) * 18 + q1_prep_bytes(cols, T) + 32 +
-           (size_t)q1::KSPLIT * q1::ROWS * T * 4;
-}
-
-// One (token t, group g) of the input -> fixed point, by one warp: lane l holds
-// inputs 4l .. 4l+3 of the group (a 16-input slice is lanes 4k .. 4k+3).
-__device__ __forceinline__ void quantise_group(float4 v, int t, int g, int groups, size_t plane, int cols, int lane,
-                                               int8_t* planes, int* ssum, float* sxg) {
-    using namespace q1;
-    float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    mx = warp_max(mx);
-    const float inv = mx > 0.0f ? (float)QMAX / mx : 0.0f;
-    if (lane == 0) sxg[(size_t)t * groups + g] = mx > 0.0f ? mx / (float)QMAX : 0.0f;
-    const float vv[4] = {v.x, v.y, v.z, v.w};
-    uint32_t dw[PLANES] = {0u, 0u, 0u};
-    int s4 = 0;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        int q = __float2int_rn(vv[e] * inv);
-        q = max(-QMAX, min(QMAX, q));
-        s4 += q;
-#pragma unroll
-        for (int p = 0; p < PLANES; ++p) {
-            const int dgt = ((q + 128) & 255) - 128;   // digit in [-128, 127]
-            dw[p] |= (uint32_t)(dgt & 0xFF) << (8 * e);
-            q = (q - dgt) >> 8;                        // exact division
-        }
-    }
-#pragma unroll
-    for (int p = 0; p < PLANES; ++p)
-        reinterpret_cast<uint32_t*>(planes + p * plane + (size_t)t * cols + (size_t)g * 128)[lane] = dw[p];
-    s4 += __shfl_xor_sync(0xffffffffu, s4, 1);
-    s4 += __shfl_xor_sync(0xffffffffu, s4, 2);
-    if ((lane & 3) == 0) ssum[((size_t)t * groups + g) * 8 + (lane >> 2)] = s4;
-}
-
-// 1. grid (ceil(groups / 8), T): one warp per (token, group)
+// ---------------------------------------------------------------------------
+// 1. input preparation: grid (ceil(groups / 8), T), one warp per (token, group)
+// ---------------------------------------------------------------------------
+// Lane l holds inputs 4l .. 4l+3 of the group.  B fragment word b0 of lane
+// (n, q) for K step s is the digits of column n at inputs 32q + s + 8b
+// (b = 0..3), word b1 the same at 32q + s + 4 + 8b.
 __global__ void __launch_bounds__(32 * q1::PREP_WARPS) q1_prep_kernel(const float* __restrict__ x, int cols, int T,
                                                                       unsigned char* __restrict__ prep) {
     using namespace q1;
@@ -111,145 +107,460 @@ __global__ void __launch_bounds__(32 * q1::PREP_WARPS) q1_prep_kernel(const floa
     const int groups = cols / 128;
     const int g = blockIdx.x * PREP_WARPS + (threadIdx.x >> 5);
     if (g >= groups) return;
-    const size_t plane = (size_t)T * cols;
-    const float4 v = reinterpret_cast<const float4*>(x + (size_t)t * cols + (size_t)g * 128)[lane];
-    quantise_group(v, t, g, groups, plane, cols, lane, reinterpret_cast<int8_t*>(prep),
-                   reinterpret_cast<int*>(prep + PLANES * plane),
-                   reinterpret_cast<float*>(prep + PLANES * plane + (size_t)T * groups * 8 * 4));
+    const int NB = q1_nb(T);
+    unsigned char* gp = prep + (size_t)g * q1_group_bytes(T);
+    const float4 v4 = reinterpret_cast<const float4*>(x + (size_t)t * cols + (size_t)g * 128)[lane];
+    const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+    float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    mx = warp_max(mx);
+    const float inv = mx > 0.0f ? (float)QMAX / mx : 0.0f;
+    int dg[PLANES][4];
+    int s4 = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        int q = __float2int_rn(v[e] * inv);
+        q = max(-QMAX, min(QMAX, q));
+        s4 += q;
+#pragma unroll
+        for (int p = 0; p < PLANES; ++p) {
+            const int dgt = ((q + 128) & 255) - 128;   // digit in [-128, 127]
+            dg[p][e] = dgt & 0xFF;
+            q = (q - dgt) >> 8;                        // exact division
+        }
+    }
+    const int S = __reduce_add_sync(0xffffffffu, s4);   // |S| <= 128 QMAX < 2^31
+    const float sx = mx > 0.0f ? mx / (float)QMAX : 0.0f;
+    // input i = 4 lane + e is K position (4 q' + b) of K step s' with
+    // q' = i / 32, s' = i % 8 (bits s', s'+8, ... of word q'), b = (i % 32) / 8
+    // -- so lane l = 8 q' + 2 b + (s' / 4) holds it at e = s' % 4 (word b0 if s' < 4, else b1)
+    uint32_t* frag = reinterpret_cast<uint32_t*>(gp);
+#pragma unroll
+    for (int p = 0; p < PLANES; ++p) {
+        const int n = 3 * t + p, nb = n >> 3, ng = n & 7;
+        // word (s, half) of fragment lane (ng, q') gathers byte e = s of lanes 8q' + 2b + half, b = 0..3
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const uint32_t mine = (uint32_t)dg[p][e];
+            const int src_q = lane >> 3, src_b = (lane >> 1) & 3, half = lane & 1;
+            // lanes with the same (q', half) build one word: OR of their bytes at position b
+            uint32_t w = mine << (8 * src_b);
+            w |= __shfl_xor_sync(0xffffffffu, w, 2);
+            w |= __shfl_xor_sync(0xffffffffu, w, 4);
+            if (src_b == 0)
+                frag[(((size_t)nb * 32 + ng * 4 + src_q) * 4 + e) * 2 + half] = w;
+        }
+    }
+    // unused columns of the last block: zero fragments and factors (written by token 0)
+    if (t == 0)
+        for (int n = 3 * T; n < 8 * NB; ++n) {
+            const int nb = n >> 3, ng = n & 7;
+            if (lane < 8) {
+                const int e = lane >> 1, half = lane & 1;
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq) frag[(((size_t)nb * 32 + ng * 4 + qq) * 4 + e) * 2 + half] = 0u;
+            }
+        }
+    // column n: block n / 8, quad (n % 8) / 2, slot n % 2
+    float* ft = reinterpret_cast<float*>(gp + (size_t)NB * 4 * 256);
+    auto ft_at = [&](int n) { return ft + ((n >> 3) * 4 + ((n & 7) >> 1)) * 4 + (n & 1); };
+    if (lane < PLANES) {
+        const int n = 3 * t + lane;
+        ft_at(n)[0] = 2.0f * (float)(1 << (8 * lane)) * sx;
+        ft_at(n)[2] = lane == 0 ? sx * (float)S : 0.0f;
+    }
+    if (t == 0 && lane < 8 * NB - 3 * T) {
+        ft_at(3 * T + lane)[0] = 0.0f;
+        ft_at(3 * T + lane)[2] = 0.0f;
+    }
 }
 
 // ---------------------------------------------------------------------------
 // 2. the GEMV
 // ---------------------------------------------------------------------------
-// TT: the launch's token count rounded up to 1, 2, 4 or 8 (register arrays sized by it)
-template <int TT>
-__global__ void __launch_bounds__(q1::THREADS, TT <= 2 ? 2 : 1) q1_gemv_kernel(Q1Desc d, const unsigned char* __restrict__ prep,
-                                                                                 int* err) {
+// Bounded wait without a suspend-time hint: the hand-offs here are short and
+// frequent, so a waiting warp should resume as soon as the phase completes.
+__device__ __forceinline__ bool q1_wait(uint64_t* bar, uint32_t parity, int* err, bool& ok) {
+    if (!ok) return false;
+    uint32_t done;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0;; ++i) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+        if (done) return true;
+        if ((i & 15u) == 15u && global_ns() - t0 > MBAR_WAIT_LIMIT_NS) break;
+    }
+    atomicExch(err, DEVERR_MBAR_TIMEOUT);
+    ok = false;
+    return false;
+}
+
+__device__ __forceinline__ void mma_s8(int* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 32-bit word at a 2-byte aligned shared-memory address
+__device__ __forceinline__ uint32_t lds_u32_a2(const unsigned char* p) {
+    const uint32_t lo = *reinterpret_cast<const unsigned short*>(p);
+    const uint32_t hi = *reinterpret_cast<const unsigned short*>(p + 2);
+    return lo | (hi << 16);
+}
+
+// float(d) for |d| < 2^22 with one integer add and one float add (the
+// conversion instruction has a quarter of the throughput): 0x4B400000 is
+// 1.5 * 2^23, whose bit pattern plus d is exactly 1.5 * 2^23 + d
+__device__ __forceinline__ float i2f_small(int d) { return __int_as_float(0x4B400000 + d) - 12582912.0f; }
+
+// shared-memory address of the same variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void arrive_cluster(uint32_t bar_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_addr) : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Work split: the row blocks are cut into equal contiguous ranges, one per
+// cluster of KS CTAs; CTA rank r of a cluster takes units
+// [r U / KS, (r+1) U / KS) of every block of its range.  Per block, every CTA
+// of the cluster stores its row sums into rank 0's reduction buffer and rank 0
+// adds them in rank order.
+template <int NB>
+__global__ void __launch_bounds__(q1::THREADS, q1::CTAS_PER_SM) q1_gemv_kernel(const __grid_constant__ Q1Desc d,
+                                                                                const unsigned char* __restrict__ prep,
+                                                                                int* err) {
     using namespace q1;
-    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int GB = NB * (4 * 256 + 64);     // prepared bytes per group
+    constexpr int XBYTES = UNIT * GB;
+    constexpr int SLOT = WBYTES + XBYTES;       // multiple of 128
+    constexpr int NCOL = 8 * NB;
+    constexpr int NT = CWARPS * 32;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int cols = d.cols, T = d.T, groups = cols / 128;
-    const int rowbytes = groups * 18;
-    int m = 0;
-    while ((int)blockIdx.x >= d.blk0[m + 1]) ++m;
-    const int r0 = ((int)blockIdx.x - d.blk0[m]) * ROWS;
-    const int nr = min(ROWS, d.rows[m] - r0);
-    const size_t prep_bytes = q1_prep_bytes(cols, T);
-    unsigned char* wsm = smem;
-    unsigned char* psm = smem + (size_t)ROWS * rowbytes;
-    const size_t plane = (size_t)T * cols;
-    const int8_t* xd = reinterpret_cast<const int8_t*>(psm);
-    const int* ssum = reinterpret_cast<const int*>(psm + PLANES * plane);
-    const float* sxg = reinterpret_cast<const float*>(psm + PLANES * plane + (size_t)T * groups * 8 * 4);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(psm + prep_bytes);   // [2]: weights, prepared input
-    float* part = reinterpret_cast<float*>(psm + prep_bytes + 32);    // [KSPLIT][ROWS][T] group-quarter sums
+    const int U = d.units, T = d.T, KS = d.ks;
+    const int clus = blockIdx.x / KS;
+    const uint32_t rank = KS > 1 ? cluster_rank() : 0u;
+    const int nclus = gridDim.x / KS, nblk = d.blk0[d.n_mats];
+    const int b_begin = clus * nblk / nclus, b_end = (clus + 1) * nblk / nclus;
+    const int u0 = (int)rank * U / KS, nu = ((int)rank + 1) * U / KS - u0;
+    const int n_it = (b_end - b_begin) * nu;
+    float* stage = reinterpret_cast<float*>(smem + NS * SLOT);          // [128][25] column sums of a block
+    float* red = stage + ROWS * 25;                                     // [KS][128][T] row sums (rank 0)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + KS * ROWS * T + ((KS * ROWS * T) & 1));
+    uint64_t* full = bars;                      // [NS] item landed
+    uint64_t* empty = full + NS;                // [NS] item read by the compute warps
+    uint64_t* red_full = empty + NS;            // rank 0: the other ranks stored their sums
+    uint64_t* red_empty = red_full + 1;         // rank > 0: rank 0 has read the buffer
 
-    if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+    auto item_of = [&](int k, int& m, int& r0, int& u) {
+        const int b = b_begin + k / nu;
+        u = u0 + k % nu;
+        m = 0;
+        while (b >= d.blk0[m + 1]) ++m;
+        r0 = (b - d.blk0[m]) * ROWS;
+    };
+    const int pre = min(NS, n_it);
+    if (warp == CWARPS && lane == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], CWARPS);
+        }
+        mbar_init(red_full, NT * (KS - 1) > 0 ? NT * (KS - 1) : 1);
+        mbar_init(red_empty, NT);
         fence_mbar_init();
-        const uint32_t bytes = (uint32_t)nr * (uint32_t)rowbytes;
-        mbar_arrive_expect_tx(&bar[0], bytes);
-        bulk_g2s(wsm, d.w[m] + (size_t)r0 * rowbytes, bytes, &bar[0]);
-        // the prepared input comes from q1_prep, this grid's programmatic predecessor
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        mbar_arrive_expect_tx(&bar[1], (uint32_t)prep_bytes);
-        bulk_g2s(psm, prep, (uint32_t)prep_bytes, &bar[1]);
-    }
-    __syncthreads();   // barrier initialisation visible to every waiting thread
-    const bool ok = mbar_wait(&bar[0], 0, err) && mbar_wait(&bar[1], 0, err);
-
-    const int sl = lane & 7;                            // 16-weight slice of each group
-    const int rb = (warp & 3) * 16 + (lane >> 3) * RL;  // this lane's first row (block-local)
-    const int kq = warp >> 2;                           // group quarter
-    const int g0 = groups * kq / KSPLIT, g1 = groups * (kq + 1) / KSPLIT;
-    float acc[RL][TT];
-#pragma unroll
-    for (int r = 0; r < RL; ++r)
-#pragma unroll
-        for (int t = 0; t < TT; ++t) acc[r][t] = 0.0f;
-    if (ok) {
-        for (int g = g0; g < g1; ++g) {
-            int wk[RL][4];
-            float sc[RL];
-#pragma unroll
-            for (int r = 0; r < RL; ++r) {
-                uint32_t bits = 0;
-                sc[r] = 0.0f;
-                if (rb + r < nr) {
-                    const unsigned char* blk = wsm + (size_t)(rb + r) * rowbytes + (size_t)g * 18;
-                    sc[r] = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(blk)));
-                    bits = *reinterpret_cast<const unsigned short*>(blk + 2 + 2 * sl);
-                }
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    wk[r][k] = (int)((((bits >> (4 * k)) & 0xFu) * 0x00204081u) & 0x01010101u);   // bit j -> byte j
-            }
-#pragma unroll
-            for (int t = 0; t < TT; ++t) {
-                if (TT == 1 || t < T) {
-                    const size_t off = (size_t)t * cols + g * 128 + 16 * sl;
-                    const int4 x0 = *reinterpret_cast<const int4*>(xd + off);
-                    const int4 x1 = *reinterpret_cast<const int4*>(xd + plane + off);
-                    const int4 x2 = *reinterpret_cast<const int4*>(xd + 2 * plane + off);
-                    const int S = ssum[((size_t)t * groups + g) * 8 + sl];
-                    const float xs = sxg[(size_t)t * groups + g];
-#pragma unroll
-                    for (int r = 0; r < RL; ++r) {
-                        int a0 = __dp4a(wk[r][0], x0.x, 0);
-                        a0 = __dp4a(wk[r][1], x0.y, a0);
-                        a0 = __dp4a(wk[r][2], x0.z, a0);
-                        a0 = __dp4a(wk[r][3], x0.w, a0);
-                        int a1 = __dp4a(wk[r][0], x1.x, 0);
-                        a1 = __dp4a(wk[r][1], x1.y, a1);
-                        a1 = __dp4a(wk[r][2], x1.z, a1);
-                        a1 = __dp4a(wk[r][3], x1.w, a1);
-                        int a2 = __dp4a(wk[r][0], x2.x, 0);
-                        a2 = __dp4a(wk[r][1], x2.y, a2);
-                        a2 = __dp4a(wk[r][2], x2.z, a2);
-                        a2 = __dp4a(wk[r][3], x2.w, a2);
-                        // |sum over set bits| <= 16 * QMAX < 2^28: 2 A - S stays inside int32
-                        const int A = (a2 * 256 + a1) * 256 + a0;
-                        acc[r][t] = fmaf(sc[r] * xs, (float)(2 * A - S), acc[r][t]);
-                    }
-                }
-            }
+        // the weights do not depend on the preceding kernel: start them before anything else
+        for (int k = 0; k < pre; ++k) {
+            int m, r0, u;
+            item_of(k, m, r0, u);
+            mbar_arrive_expect_tx(&full[k], SLOT);
+            tc::tma_load_2d(smem + k * SLOT, &d.map[m], u * UNIT_BYTES, r0, &full[k]);
         }
     }
-#pragma unroll
-    for (int r = 0; r < RL; ++r)
-#pragma unroll
-        for (int t = 0; t < TT; ++t) {
-            float v = acc[r][t];
-            v += __shfl_xor_sync(0xffffffffu, v, 1);
-            v += __shfl_xor_sync(0xffffffffu, v, 2);
-            v += __shfl_xor_sync(0xffffffffu, v, 4);
-            acc[r][t] = v;
-        }
-    if (sl == 0) {
-#pragma unroll
-        for (int r = 0; r < RL; ++r)
-#pragma unroll
-            for (int t = 0; t < TT; ++t)
-                if (t < T) part[((size_t)kq * ROWS + rb + r) * T + t] = acc[r][t];
-    }
+    // barrier initialisation visible to the whole cluster before any remote arrive:
+    // every thread arrives now and waits only before its first remote access
+    if (KS > 1) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     __syncthreads();
-    if (ok) {
-        const int rows = d.rows[m];
-        for (int i = tid; i < nr * T; i += THREADS) {
-            const int r = i / T, t = i - r * T;
-            float v = part[(size_t)r * T + t];
+    bool ok = true;
+
+    if (warp == CWARPS) {
+        // ---------------- loads (one thread) ----------------
+        if (lane == 0) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int k = 0; k < pre; ++k) {
+                int m, r0, u;
+                item_of(k, m, r0, u);
+                bulk_g2s(smem + k * SLOT + WBYTES, prep + (size_t)u * XBYTES, XBYTES, &full[k]);
+            }
+            int k = pre;
+            for (; k < n_it; ++k) {
+                const int s = k % NS;
+                if (!q1_wait(&empty[s], ((k / NS) - 1) & 1, err, ok)) break;
+                int m, r0, u;
+                item_of(k, m, r0, u);
+                mbar_arrive_expect_tx(&full[s], SLOT);
+                tc::tma_load_2d(smem + s * SLOT, &d.map[m], u * UNIT_BYTES, r0, &full[s]);
+                bulk_g2s(smem + s * SLOT + WBYTES, prep + (size_t)u * XBYTES, XBYTES, &full[s]);
+            }
+            // copies still in flight when a wait gave up land before the CTA exits
+            if (!ok)
+                for (int j = max(0, k - NS); j < k; ++j) mbar_wait(&full[j % NS], (j / NS) & 1, err);
+        }
+        __syncwarp();
+        if (KS > 1) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    } else {
+        // ---------------- compute: warp w owns rows 16w .. 16w+15 of each item ----------------
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        const int g = lane >> 2, q = lane & 3;
+        const int rA = 16 * warp + g, rB = rA + 8;
+        float acc[NB][4];
 #pragma unroll
-            for (int k = 1; k < KSPLIT; ++k) v += part[((size_t)k * ROWS + r) * T + t];
-            float* yp = d.y[m] + (size_t)t * rows + r0 + r;
-            *yp = d.accumulate ? *yp + v : v;
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
+
+        // a block's sums are complete: rank 0 of the cluster writes y
+        auto flush = [&](int k, int blk_idx) {
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+                stage[rA * 25 + nb * 8 + 2 * q] = acc[nb][0];
+                stage[rA * 25 + nb * 8 + 2 * q + 1] = acc[nb][1];
+                stage[rB * 25 + nb * 8 + 2 * q] = acc[nb][2];
+                stage[rB * 25 + nb * 8 + 2 * q + 1] = acc[nb][3];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
+            }
+            tc::named_bar_sync(1, NT);
+            int m, r0, u;
+            item_of(k, m, r0, u);
+            const int rows = d.rows[m];
+            const int nr = min(ROWS, rows - r0);
+            float* yb = d.y[m] + r0;
+            const int r = tid;                                   // threads 0..127: one row each
+            float v[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[t] = 0.0f;
+            if (r < ROWS)
+#pragma unroll
+                for (int t = 0; t < 8; ++t)
+                    if (3 * t + 2 < NCOL && t < T)
+                        v[t] = stage[r * 25 + 3 * t] + stage[r * 25 + 3 * t + 1] + stage[r * 25 + 3 * t + 2];
+            if (KS == 1) {
+                if (r < nr)
+#pragma unroll
+                    for (int t = 0; t < 8; ++t)
+                        if (t < T) {
+                            float* yp = yb + (size_t)t * rows + r;
+                            *yp = d.accumulate ? *yp + v[t] : v[t];
+                        }
+            } else if (rank != 0) {
+                if (blk_idx == 0) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+                // the buffer is free once rank 0 has read the previous block
+                if (blk_idx > 0) ok = __all_sync(0xffffffffu, q1_wait(red_empty, (blk_idx - 1) & 1, err, ok));
+                if (r < ROWS) {
+                    const uint32_t dst = cluster_addr(red + ((size_t)rank * ROWS + r) * T, 0);
+#pragma unroll
+                    for (int t = 0; t < 8; ++t)
+                        if (t < T) st_cluster_f32(dst + 4 * t, v[t]);
+                }
+                arrive_cluster(cluster_addr(red_full, 0));
+            } else {
+                if (blk_idx == 0) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+                ok = __all_sync(0xffffffffu, q1_wait(red_full, blk_idx & 1, err, ok));
+                if (r < ROWS) {
+                    float sum[8];
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) sum[t] = v[t];
+                    for (int rr = 1; rr < KS; ++rr) {
+                        const float* pr = red + ((size_t)rr * ROWS + r) * T;
+#pragma unroll
+                        for (int t = 0; t < 8; ++t)
+                            if (t < T) sum[t] += pr[t];
+                    }
+                    if (r < nr)
+#pragma unroll
+                        for (int t = 0; t < 8; ++t)
+                            if (t < T) {
+                                float* yp = yb + (size_t)t * rows + r;
+                                *yp = d.accumulate ? *yp + sum[t] : sum[t];
+                            }
+                }
+                // the other ranks may overwrite their parts now (after the last block
+                // nothing touches their shared memory any more, so they may exit)
+                if (blk_idx < (b_end - b_begin) - 1)
+                    for (int rr = 1; rr < KS; ++rr) arrive_cluster(cluster_addr(red_empty, (uint32_t)rr));
+            }
+            tc::named_bar_sync(1, NT);                           // stage free for the next block
+        };
+
+        for (int k = 0; k < n_it; ++k) {
+            const int s = k % NS;
+            ok = __all_sync(0xffffffffu, q1_wait(&full[s], (k / NS) & 1, err, ok));
+            const unsigned char* wA = smem + s * SLOT + rA * UNIT_BYTES;
+            const unsigned char* wB = smem + s * SLOT + rB * UNIT_BYTES;
+            const unsigned char* xp = smem + s * SLOT + WBYTES;
+#pragma unroll
+            for (int j = 0; j < UNIT; ++j) {
+                // row scales (binary16 at byte 18j) and sign word q (bytes 18j + 2 + 4q:
+                // 4-byte aligned for odd j)
+                const float scA = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(wA + 18 * j)));
+                const float scB = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(wB + 18 * j)));
+                uint32_t swA, swB;
+                if (j % 2 == 1) {
+                    swA = *reinterpret_cast<const uint32_t*>(wA + 18 * j + 2 + 4 * q);
+                    swB = *reinterpret_cast<const uint32_t*>(wB + 18 * j + 2 + 4 * q);
+                } else {
+                    swA = lds_u32_a2(wA + 18 * j + 2 + 4 * q);
+                    swB = lds_u32_a2(wB + 18 * j + 2 + 4 * q);
+                }
+                const unsigned char* gp = xp + j * GB;
+                int dacc[NB][4];
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    // this lane's B fragments of the 4 K steps
+                    const uint4 f01 = reinterpret_cast<const uint4*>(gp)[(nb * 32 + lane) * 2];
+                    const uint4 f23 = reinterpret_cast<const uint4*>(gp)[(nb * 32 + lane) * 2 + 1];
+                    const uint32_t bw[8] = {f01.x, f01.y, f01.z, f01.w, f23.x, f23.y, f23.z, f23.w};
+                    // K steps 0, 1 and 2, 3 as two independent accumulation chains
+                    int dk[2][4];
+#pragma unroll
+                    for (int st = 0; st < 4; ++st) {
+                        if (st < 2)
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) dk[st][i] = 0;
+                        const uint32_t a0 = (swA >> st) & 0x01010101u, a2 = (swA >> (st + 4)) & 0x01010101u;
+                        const uint32_t a1 = (swB >> st) & 0x01010101u, a3 = (swB >> (st + 4)) & 0x01010101u;
+                        mma_s8(dk[st & 1], a0, a1, a2, a3, bw[2 * st], bw[2 * st + 1]);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) dacc[nb][i] = dk[0][i] + dk[1][i];
+                }
+                const float4* ft = reinterpret_cast<const float4*>(gp + NB * 4 * 256);
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    const float4 f = ft[nb * 4 + q];                 // factor pair, term pair
+                    acc[nb][0] = fmaf(scA, fmaf(f.x, i2f_small(dacc[nb][0]), -f.z), acc[nb][0]);
+                    acc[nb][1] = fmaf(scA, fmaf(f.y, i2f_small(dacc[nb][1]), -f.w), acc[nb][1]);
+                    acc[nb][2] = fmaf(scB, fmaf(f.x, i2f_small(dacc[nb][2]), -f.z), acc[nb][2]);
+                    acc[nb][3] = fmaf(scB, fmaf(f.y, i2f_small(dacc[nb][3]), -f.w), acc[nb][3]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&empty[s]);
+            if (k % nu == nu - 1) flush(k, k / nu);
         }
     }
+    // Rank 0 leaves after the other ranks' last stores and arrivals reached it;
+    // the other ranks' shared memory is not accessed after their last block.
+}
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+// tensor maps of recently used weight matrices: (base, rows, row bytes) -> map
+struct Q1MapCache {
+    struct Entry {
+        const void* base = nullptr;
+        int rows = 0, rowbytes = 0;
+        CUtensorMap map;
+    };
+    Entry e[32];
+    int next = 0;
+};
+
+void free_q1_maps(dz_ctx* ctx) {
+    delete static_cast<Q1MapCache*>(ctx->q1_maps);
+    ctx->q1_maps = nullptr;
+}
+
+static bool q1_map(dz_ctx* ctx, const uint8_t* base, int rows, int rowbytes, CUtensorMap* out) {
+    if (!ctx->q1_maps) ctx->q1_maps = new Q1MapCache();
+    Q1MapCache* cache = static_cast<Q1MapCache*>(ctx->q1_maps);
+    for (auto& en : cache->e)
+        if (en.base == base && en.rows == rows && en.rowbytes == rowbytes) {
+            *out = en.map;
+            return true;
+        }
+    EncodeTiledFn fn = tensor_map_encoder();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)rowbytes, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)rowbytes};
+    cuuint32_t box[2] = {(cuuint32_t)q1::UNIT_BYTES, (cuuint32_t)q1::ROWS};
+    cuuint32_t estr[2] = {1, 1};
+    Q1MapCache::Entry& en = cache->e[cache->next];
+    if (fn(&en.map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        en.base = nullptr;
+        return false;
+    }
+    en.base = base;
+    en.rows = rows;
+    en.rowbytes = rowbytes;
+    cache->next = (cache->next + 1) % 32;
+    *out = en.map;
+    return true;
+}
+
+template <int NB>
+static cudaError_t launch_gemv(const Q1Desc& d, int G, size_t smem, const unsigned char* prep, int* err,
+                               cudaStream_t st) {
+    auto kern = q1_gemv_kernel<NB>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = (unsigned)d.ks;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(G);
+    lc.blockDim = dim3(q1::THREADS);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    lc.attrs = at;
+    lc.numAttrs = 2;
+    return cudaLaunchKernelEx(&lc, kern, d, prep, err);
+}
+
+// CTAs per cluster for nblk row blocks of U units on `slots` resident CTAs: the
+// fewest items per CTA, ceil(nblk / clusters) * ceil(U / ks), smallest ks on ties
+static int q1_pick_ks(int nblk, int U, int slots) {
+    int best = 1;
+    long best_items = -1;
+    for (int ks = 1; ks <= std::min(Q1_MAX_KS, U); ks *= 2) {
+        const int nclus = std::max(1, std::min(nblk, slots / ks));
+        // + one item's time for the cross-CTA reduction of a cluster
+        const long items = (long)((nblk + nclus - 1) / nclus) * ((U + ks - 1) / ks) + (ks > 1 ? 1 : 0);
+        if (best_items < 0 || items < best_items) {
+            best_items = items;
+            best = ks;
+        }
+    }
+    return best;
 }
 
 cudaError_t launch_q1_gemv(dz_ctx* ctx, int n_mats, const uint8_t* const* w, const int32_t* rows, int cols, int T,
                            const float* x, float* const* y, bool accumulate, cudaStream_t st, int* n_launch) {
-    cudaError_t e = ensure_q1_scratch(ctx, q1_prep_bytes(cols, T));
+    const int groups = cols / 128;
+    const size_t need = (size_t)groups * q1_group_bytes(T);
+    cudaError_t e = ensure_q1_scratch(ctx, need);
     if (e != cudaSuccess) return e;
     unsigned char* prep = static_cast<unsigned char*>(ctx->q1);
     Q1Desc d{};
@@ -257,30 +568,28 @@ cudaError_t launch_q1_gemv(dz_ctx* ctx, int n_mats, const uint8_t* const* w, con
     d.cols = cols;
     d.T = T;
     d.accumulate = accumulate ? 1 : 0;
+    d.units = groups / q1::UNIT;
     d.blk0[0] = 0;
     for (int m = 0; m < n_mats; ++m) {
-        d.w[m] = w[m];
+        if (!q1_map(ctx, w[m], rows[m], groups * 18, &d.map[m])) return cudaErrorInvalidValue;
         d.y[m] = y[m];
         d.rows[m] = rows[m];
         d.blk0[m + 1] = d.blk0[m] + (rows[m] + q1::ROWS - 1) / q1::ROWS;
     }
     for (int m = n_mats; m < Q1_MAX_MATS; ++m) d.blk0[m + 1] = d.blk0[n_mats];
-    const int smem = (int)q1_smem_bytes(cols, T);
-    auto kern = T <= 1 ? q1_gemv_kernel<1> : T <= 2 ? q1_gemv_kernel<2> : T <= 4 ? q1_gemv_kernel<4> : q1_gemv_kernel<8>;
-    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
-    q1_prep_kernel<<<dim3((cols / 128 + q1::PREP_WARPS - 1) / q1::PREP_WARPS, T), 32 * q1::PREP_WARPS, 0, st>>>(
-        x, cols, T, prep);
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t lc{};
-    lc.gridDim = dim3(d.blk0[n_mats]);
-    lc.blockDim = dim3(q1::THREADS);
-    lc.dynamicSmemBytes = smem;
-    lc.stream = st;
-    lc.attrs = at;
-    lc.numAttrs = 1;
-    e = cudaLaunchKernelEx(&lc, kern, d, (const unsigned char*)prep, ctx->d_err);
+    const int nblk = d.blk0[n_mats];
+    const int slots = q1::CTAS_PER_SM * ctx->n_sm;
+    d.ks = q1_pick_ks(nblk, d.units, slots);
+    const int nclus = std::max(1, std::min(nblk, slots / d.ks));
+    const int G = nclus * d.ks;
+    const size_t smem = q1_smem_bytes(cols, T) - (size_t)(Q1_MAX_KS - d.ks) * q1::ROWS * T * 4;
+    q1_prep_kernel<<<dim3((groups + q1::PREP_WARPS - 1) / q1::PREP_WARPS, T), 32 * q1::PREP_WARPS, 0, st>>>(x, cols, T,
+                                                                                                            prep);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const int NB = q1_nb(T);
+    if (NB == 1) e = launch_gemv<1>(d, G, smem, prep, ctx->d_err, st);
+    else if (NB == 2) e = launch_gemv<2>(d, G, smem, prep, ctx->d_err, st);
+    else e = launch_gemv<3>(d, G, smem, prep, ctx->d_err, st);
     if (e != cudaSuccess) return e;
     *n_launch += 2;
     return cudaGetLastError();

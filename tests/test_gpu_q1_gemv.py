@@ -49,7 +49,8 @@ def test_q1_gemv_projection_sets(ctx, rows, T):
     assert ctx.device_error() == 0
 
 
-@pytest.mark.parametrize("rows,cols,T", [((100, 7), 1024, 8), ((65,), 17408, 1), ((64, 1, 129), 2048, 2)])
+@pytest.mark.parametrize("rows,cols,T", [((100, 7), 1024, 8), ((65,), 17408, 1), ((64, 1, 129), 2048, 2),
+                                         ((5120,), 17408, 8), ((300, 2000), 3072, 6)])
 def test_q1_gemv_ragged_and_wide(ctx, rows, cols, T):
     seed = O.SEED0 + 7100 + cols + T
     ws = [O.q1_random(seed + 10 * i, r, cols) for i, r in enumerate(rows)]
@@ -85,7 +86,7 @@ def test_q1_gemv_rejects_bad_arguments(ctx):
     with pytest.raises(DzError) as e:                    # weights not 16-byte aligned
         ctx.q1_gemv([w.view(-1)[8:8 + 63 * 288].view(63, 288)], x, [y])
     assert e.value.status == DZ_EINVAL
-    wide = torch.zeros(64, 17408 // 128 * 18, dtype=torch.uint8, device="cuda")
-    with pytest.raises(DzError) as e:                    # 17408 columns x 8 tokens do not fit one CTA
-        ctx.q1_gemv([wide], torch.zeros(8, 17408, device="cuda"), [torch.empty(8, 64, device="cuda")])
+    tall = torch.zeros(4097 * 128, 1024 // 128 * 18, dtype=torch.uint8, device="cuda")
+    with pytest.raises(DzError) as e:                    # more than 4096 blocks of 128 rows in one call
+        ctx.q1_gemv([tall], torch.zeros(1, 1024, device="cuda"), [torch.empty(1, 4097 * 128, device="cuda")])
     assert e.value.status == DZ_EINVAL
