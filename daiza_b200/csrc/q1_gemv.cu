@@ -179,16 +179,24 @@ __global__ void __launch_bounds__(32 * q1::PREP_WARPS) q1_prep_kernel(const floa
 // ---------------------------------------------------------------------------
 // Bounded wait without a suspend-time hint: the hand-offs here are short and
 // frequent, so a waiting warp should resume as soon as the phase completes.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool q1_wait(uint64_t* bar, uint32_t parity, int* err, bool& ok) {
     if (!ok) return false;
     uint32_t done;
     const uint64_t t0 = global_ns();
     for (uint32_t i = 0;; ++i) {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+        if (CLUSTER)
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+        else
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
         if (done) return true;
         if ((i & 15u) == 15u && global_ns() - t0 > MBAR_WAIT_LIMIT_NS) break;
     }
@@ -280,8 +288,8 @@ __global__ void __launch_bounds__(q1::THREADS, q1::CTAS_PER_SM) q1_gemv_kernel(c
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], CWARPS);
         }
-        mbar_init(red_full, NT * (KS - 1) > 0 ? NT * (KS - 1) : 1);
-        mbar_init(red_empty, NT);
+        mbar_init(red_full, CWARPS * (KS - 1) > 0 ? CWARPS * (KS - 1) : 1);
+        mbar_init(red_empty, CWARPS);
         fence_mbar_init();
         // the weights do not depend on the preceding kernel: start them before anything else
         for (int k = 0; k < pre; ++k) {
@@ -370,17 +378,19 @@ __global__ void __launch_bounds__(q1::THREADS, q1::CTAS_PER_SM) q1_gemv_kernel(c
             } else if (rank != 0) {
                 if (blk_idx == 0) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
                 // the buffer is free once rank 0 has read the previous block
-                if (blk_idx > 0) ok = __all_sync(0xffffffffu, q1_wait(red_empty, (blk_idx - 1) & 1, err, ok));
+                if (blk_idx > 0) ok = __all_sync(0xffffffffu, q1_wait<true>(red_empty, (blk_idx - 1) & 1, err, ok));
                 if (r < ROWS) {
                     const uint32_t dst = cluster_addr(red + ((size_t)rank * ROWS + r) * T, 0);
 #pragma unroll
                     for (int t = 0; t < 8; ++t)
                         if (t < T) st_cluster_f32(dst + 4 * t, v[t]);
                 }
-                arrive_cluster(cluster_addr(red_full, 0));
+                // one release per warp covers the warp's stores (ordered by the warp barrier)
+                __syncwarp();
+                if (lane == 0) arrive_cluster(cluster_addr(red_full, 0));
             } else {
                 if (blk_idx == 0) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-                ok = __all_sync(0xffffffffu, q1_wait(red_full, blk_idx & 1, err, ok));
+                ok = __all_sync(0xffffffffu, q1_wait<true>(red_full, blk_idx & 1, err, ok));
                 if (r < ROWS) {
                     float sum[8];
 #pragma unroll
@@ -401,7 +411,8 @@ __global__ void __launch_bounds__(q1::THREADS, q1::CTAS_PER_SM) q1_gemv_kernel(c
                 }
                 // the other ranks may overwrite their parts now (after the last block
                 // nothing touches their shared memory any more, so they may exit)
-                if (blk_idx < (b_end - b_begin) - 1)
+                __syncwarp();
+                if (blk_idx < (b_end - b_begin) - 1 && lane == 0)
                     for (int rr = 1; rr < KS; ++rr) arrive_cluster(cluster_addr(red_empty, (uint32_t)rr));
             }
             tc::named_bar_sync(1, NT);                           // stage free for the next block
