@@ -23,6 +23,10 @@ Extra keys on the same line:
   q1_gemv            the Q1_0 input-projection GEMV that feeds the cores (hidden
                      5120, 1 and 4 tokens) and the block tail after them
                      (post-norm + SwiGLU MLP, d_ff 17408); N = 1 only
+  block              whole decoder blocks for one sequence and one token (norm,
+                     projections, core, output projection, MLP) and their
+                     64-layer sum beside the reference's published per-token
+                     decode times; N = 1 only
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -633,6 +637,101 @@ def bench_q1(dz, torch, local, tokens=(1, 4)):
                              "sample": "attention input projection set, 1 token, dot_q1_0_row over all rows"}}
 
 
+BLOCK_LAYERS = 16            # 8 gated GQA + 8 Gated DeltaNet layers, each with its own weights
+BLOCK_POS = 2048             # KV positions cached in front of the timed tokens (config 0)
+PUBLISHED_MS = {"attn16": 11.5, "gdn48": 38.5, "model": 143.0}   # reference README.md:431-439, per token
+
+
+def bench_block(dz, torch, local):
+    """Whole decoder blocks, one sequence, one token (the reference's decode
+    step): rmsnorm -> Q1_0 input projections -> core -> Q1_0 output projection
+    added into h -> post-norm SwiGLU MLP added into h, all through the public
+    entry points.  8 layers of each kind with distinct synthetic weights (~52 MB
+    per block, ~850 MB in all > L2), captured per kind in one CUDA graph and
+    replayed; the GQA layers hold 2048 cached positions.  The 64-layer figure is
+    16 x GQA block + 48 x DeltaNet block (embedding, final norm and LM head
+    excluded), beside the reference's published per-token times on its CPU."""
+    import oracle as O
+    dev = torch.device("cuda", local)
+    ctx = dz.Context(local, dz.default_config(n_layers=BLOCK_LAYERS, full_attention_interval=2))
+    (qn, kn), sp = layer_params(SEED0 + 7)
+    ctx.cache_create([BLOCK_POS + 64])
+    hbm, _, kind = peaks()
+    base = {
+        "attn_norm": torch.ones(Q1_HIDDEN, device=dev), "post_norm": torch.ones(Q1_HIDDEN, device=dev),
+        "gate": O.q1_random(SEED0 + 970, Q1_FF, Q1_HIDDEN), "up": O.q1_random(SEED0 + 971, Q1_FF, Q1_HIDDEN),
+        "down": O.q1_random(SEED0 + 972, Q1_HIDDEN, Q1_FF, 0.01),
+        "out": O.q1_random(SEED0 + 973, Q1_HIDDEN, HQ * HD, 0.01),
+        "attn_proj": [O.q1_random(SEED0 + 974 + i, r, Q1_HIDDEN) for i, r in enumerate(Q1_SETS[0][1])],
+        "gdn_proj": [O.q1_random(SEED0 + 978 + i, r, Q1_HIDDEN) for i, r in enumerate(Q1_SETS[1][1])],
+    }
+    layers = []
+    for layer in range(BLOCK_LAYERS):
+        attn = ctx.is_attention(layer)
+        if attn:
+            ctx.set_attn_params(layer, qn, kn)
+            ctx.kv_fill_pattern(layer, 0, BLOCK_POS)
+        else:
+            ctx.set_ssm_params(layer, *sp)
+        proj = base["attn_proj"] if attn else base["gdn_proj"]
+        layers.append({"attn": attn,
+                       "proj": [torch.from_numpy(x).to(dev) for x in proj],
+                       "out": torch.from_numpy(base["out"]).to(dev),
+                       "gate": torch.from_numpy(base["gate"]).to(dev), "up": torch.from_numpy(base["up"]).to(dev),
+                       "down": torch.from_numpy(base["down"]).to(dev)})
+    wbytes = {a: sum(x.nbytes for x in (base["attn_proj"] if a else base["gdn_proj"])) + base["out"].nbytes
+              + base["gate"].nbytes + base["up"].nbytes + base["down"].nbytes for a in (True, False)}
+    h = torch.randn(1, Q1_HIDDEN, device=dev)
+    normed = torch.empty_like(h)
+    core = torch.empty(1, HQ * HD, device=dev)
+    bufs = {a: [torch.empty(1, r, device=dev) for r in (Q1_SETS[0][1] if a else Q1_SETS[1][1])] for a in (True, False)}
+
+    def block(L, li):
+        ctx.rmsnorm_rows(h, base["attn_norm"], normed)
+        p = bufs[L["attn"]]
+        ctx.q1_gemv(L["proj"], normed, p)
+        if L["attn"]:
+            ctx.gqa_decode(li, [0], p[0], p[1], p[2], core)
+        else:
+            ctx.gdn_decode(li, [0], p[0], p[1], p[2], p[3], core)
+        ctx.q1_gemv_add([L["out"]], core, [h])
+        ctx.block_mlp(h, base["post_norm"], L["gate"], L["up"], L["down"])
+
+    out = {}
+    for attn in (True, False):
+        idx = [i for i in range(BLOCK_LAYERS) if layers[i]["attn"] == attn]
+        block(layers[idx[0]], idx[0])            # warm-up outside the graph (scratch allocation)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in idx:
+                block(layers[i], i)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / (reps * len(idx))
+        core_bytes = (gqa_bytes([BLOCK_POS + 8]) if attn else gdn_bytes(1))
+        nbytes = wbytes[attn] + core_bytes
+        out["gqa_block" if attn else "gdn_block"] = {
+            "us": us, "weight_mb": wbytes[attn] / 1e6, "core_mb": core_bytes / 1e6, "gbs": nbytes / us / 1e3,
+            "frac": nbytes / us / 1e3 / hbm, "peak_kind": f"{kind} hbm_gbs", "layers_timed": len(idx)}
+        del graph
+    a_us, g_us = out["gqa_block"]["us"], out["gdn_block"]["us"]
+    out["per_token_ms"] = {"attn16": 16 * a_us / 1e3, "gdn48": 48 * g_us / 1e3, "blocks64": (16 * a_us + 48 * g_us) / 1e3}
+    out["reference_published_ms"] = dict(PUBLISHED_MS,
+                                         note="README.md:431-439, Core Ultra 5 225H CPU, whole model incl. LM head")
+    out["device_error"] = ctx.device_error()
+    ctx.close()
+    return out
+
+
 PF_T = 8192
 
 
@@ -823,6 +922,8 @@ def run_ours(args):
         extra["prefill"] = bench_prefill(dz, torch, local, args)
     if world == 1 and not args.no_q1:
         extra["q1_gemv"] = bench_q1(dz, torch, local)
+        torch.cuda.empty_cache()
+        extra["block"] = bench_block(dz, torch, local)
     if not args.no_stack:
         torch.cuda.empty_cache()
         extra["stack"] = bench_stack(dz, torch, dist, dev, local, rank, world, args)

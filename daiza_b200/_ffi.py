@@ -57,6 +57,7 @@ SIGNATURES = {
     "dz_q1_gemv": [_P, _I, _P, _P, _I, _I, _P, _P, _P],
     "dz_q1_gemv_add": [_P, _I, _P, _P, _I, _I, _P, _P, _P],
     "dz_block_mlp": [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P],
+    "dz_rmsnorm_rows": [_P, _I, _I, _P, _P, _P, _P],
     "dz_session_save": [_P, _I, C.c_char_p, _I64, _P, _I64, _I, C.c_char_p],
     "dz_session_load": [_P, _I, C.c_char_p, _P, _P, _I64, _P, _P, _P, _I64, _P],
     "dz_snapshot_reserve": [_P, _I],

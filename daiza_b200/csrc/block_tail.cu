@@ -13,6 +13,7 @@ namespace dz {
 __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                            float eps, int n, float* __restrict__ out) {
     __shared__ float red[8];
+    asm volatile("griddepcontrol.launch_dependents;");
     const int row = blockIdx.x, tid = threadIdx.x;
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * n);
     float ss = 0.0f;
@@ -36,6 +37,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
 }
 
 __global__ void swiglu_kernel(float* __restrict__ gate, const float* __restrict__ up, int64_t n4) {
+    asm volatile("griddepcontrol.launch_dependents;");
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
         float4 g = reinterpret_cast<float4*>(gate)[i];
         const float4 u = reinterpret_cast<const float4*>(up)[i];

@@ -599,6 +599,20 @@ dz_status dz_q1_gemv_add(dz_ctx* ctx, int n_mats, const void* const* w, const in
     return st;
 }
 
+dz_status dz_rmsnorm_rows(dz_ctx* ctx, int T, int n, const float* x, const float* w, float* out, void* stream) {
+    if (!ctx) return DZ_EINVAL;
+    if (T < 1 || n < 4 || n % 4 != 0) return fail(ctx, DZ_EINVAL, "T=%d, n=%d: need T >= 1 and n a multiple of 4", T, n);
+    if (!x || !w || !out) return fail(ctx, DZ_EINVAL, "null argument");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) % 16 != 0)
+        return fail(ctx, DZ_EINVAL, "x, w and out must be 16-byte aligned");
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    cudaError_t e = launch_rmsnorm_rows(x, w, ctx->cfg.rms_eps, T, n, out, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "rmsnorm launch");
+    ctx->last_launches = 1;
+    return DZ_OK;
+}
+
 // ---------------------------------------------------------------------------
 // block MLP (block.rs:93-124 + mlp.rs:28-58)
 // ---------------------------------------------------------------------------

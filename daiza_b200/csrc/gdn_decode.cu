@@ -164,6 +164,7 @@ __global__ void __launch_bounds__(256, STATE_CPS) gdn_dec_state_kernel(GdnDecode
                                                                       int* err) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     GdnSmem& sm = *reinterpret_cast<GdnSmem*>(smem_raw);
+    asm volatile("griddepcontrol.launch_dependents;");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 3, c = lane & 7;   // row within a 4-row group, column lane
     auto state_ptr = [&](int item) {
@@ -315,6 +316,8 @@ __global__ void __launch_bounds__(32 * (SSM_D / RS / 8)) gdn_dec_kernel(
     constexpr int ROWS = Smem::ROWS;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+    // a programmatic successor (the next projection) may start streaming its weights
+    asm volatile("griddepcontrol.launch_dependents;");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int item = blockIdx.x / RS;                 // b * vc + vl
     const int rank = (int)cluster_rank();             // == blockIdx.x % RS

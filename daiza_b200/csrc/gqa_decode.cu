@@ -373,6 +373,8 @@ __global__ void __launch_bounds__(32 * CMB_MAX_GROUPS) gqa_combine_kernel(GqaDec
                                                                           float* __restrict__ out) {
     __shared__ float wgt[MAXC];
     __shared__ float red[2][CMB_MAX_GROUPS];
+    // a programmatic successor (the next projection) may start streaming its weights
+    asm volatile("griddepcontrol.launch_dependents;");
     __shared__ __align__(16) float acc_s[CMB_MAX_GROUPS][HD];
     const int nq = GRP * kvc;
     const int qh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;

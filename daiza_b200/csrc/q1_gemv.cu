@@ -102,7 +102,10 @@ struct Q1Desc {
 __global__ void __launch_bounds__(32 * q1::PREP_WARPS) q1_prep_kernel(const float* __restrict__ x, int cols, int T,
                                                                       unsigned char* __restrict__ prep) {
     using namespace q1;
+    // the GEMV may start (and stream its weights) now; x and the scratch it reads are
+    // the predecessor's, so wait for that grid before touching them
     asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int t = blockIdx.y, lane = threadIdx.x & 31;
     const int groups = cols / 128;
     const int g = blockIdx.x * PREP_WARPS + (threadIdx.x >> 5);
@@ -594,9 +597,20 @@ cudaError_t launch_q1_gemv(dz_ctx* ctx, int n_mats, const uint8_t* const* w, con
     const int nclus = std::max(1, std::min(nblk, slots / d.ks));
     const int G = nclus * d.ks;
     const size_t smem = q1_smem_bytes(cols, T) - (size_t)(Q1_MAX_KS - d.ks) * q1::ROWS * T * 4;
-    q1_prep_kernel<<<dim3((groups + q1::PREP_WARPS - 1) / q1::PREP_WARPS, T), 32 * q1::PREP_WARPS, 0, st>>>(x, cols, T,
-                                                                                                            prep);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    {
+        // a programmatic dependent of whatever precedes it on the stream (it waits for
+        // that grid inside), so the GEMV's weight loads can start while it finishes
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t lc{};
+        lc.gridDim = dim3((groups + q1::PREP_WARPS - 1) / q1::PREP_WARPS, T);
+        lc.blockDim = dim3(32 * q1::PREP_WARPS);
+        lc.stream = st;
+        lc.attrs = at;
+        lc.numAttrs = 1;
+        if ((e = cudaLaunchKernelEx(&lc, q1_prep_kernel, x, cols, T, prep)) != cudaSuccess) return e;
+    }
     const int NB = q1_nb(T);
     if (NB == 1) e = launch_gemv<1>(d, G, smem, prep, ctx->d_err, st);
     else if (NB == 2) e = launch_gemv<2>(d, G, smem, prep, ctx->d_err, st);

@@ -152,6 +152,11 @@ class Context:
         self._chk(self.lib.dz_q1_gemv_add(self.h, len(ws), C.cast(wp, C.c_void_p), _np_ptr(rows), cols, T, _ptr(x),
                                           C.cast(yp, C.c_void_p), _stream(stream)))
 
+    def rmsnorm_rows(self, x, w, out, stream=None):
+        """math::rmsnorm_into per row of x [T][n] into out (the context's rms_eps)."""
+        T, n = x.shape
+        self._chk(self.lib.dz_rmsnorm_rows(self.h, T, n, _ptr(x), _ptr(w), _ptr(out), _stream(stream)))
+
     def block_mlp(self, h, post_norm_w, w_gate, w_up, w_down, stream=None):
         """block.rs:93-124 + mlp.rs:28-51 on h [T][hidden] in place."""
         T, hidden = h.shape

@@ -220,6 +220,15 @@ dz_status dz_snapshot_restore(dz_ctx* ctx, int seq, int slot, void* stream);
 dz_status dz_q1_gemv_add(dz_ctx* ctx, int n_mats, const void* const* w, const int32_t* rows, int cols, int T,
                          const float* x, float* const* y, void* stream);
 
+/* ---- block entry norm ------------------------------------------------------- */
+/* math::rmsnorm_into (math/rmsnorm.rs:85-140, 180-202) per row: out[t] =
+ * (x[t] * inv_rms) * w with inv_rms = 1 / sqrt(sum x[t]^2 / n + eps) -- the
+ * attn_norm in front of a block's input projections (attention.rs:72,
+ * ssm.rs:443) and the post_attention_norm (block.rs:101).  x, out: device
+ * [T][n] f32, w: device [n] f32, all 16-byte aligned; n a multiple of 4;
+ * eps = the context's rms_eps. */
+dz_status dz_rmsnorm_rows(dz_ctx* ctx, int T, int n, const float* x, const float* w, float* out, void* stream);
+
 /* ---- block tail: post-norm + SwiGLU MLP ------------------------------------ */
 /* The rest of a block after the attention / Gated DeltaNet output projection
  * (model/block.rs:93-124 with mlp.rs:28-51), for T <= 8 tokens:
