@@ -71,6 +71,8 @@ SIGNATURES = {
     "dz_gdn_prefill": [_P, _I, _I, _I64, _P, _P, _P, _P, _P, _P],
     "dz_gqa_decode_host": [_P, _I, _I, _P, _P, _P, _P, _P, _P],
     "dz_gdn_decode_host": [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P],
+    "dz_gqa_decode_host_async": [_P, _I, _I, _P, _P, _P, _P, _P, _P],
+    "dz_gdn_decode_host_async": [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P],
     "dz_gqa_decode_noalloc": [_P, _I, _I, _P, _P, _P, _P, _P, _P],
     "dz_last_launch_count": [_P],
     "dz_device_error": [_P, C.POINTER(C.c_int32)],

@@ -256,6 +256,12 @@ dz_status dz_ctx_destroy(dz_ctx* ctx) {
         if (ctx->snap_mem) cudaFree(ctx->snap_mem);
         for (auto& e : ctx->pf_ev)
             if (e) cudaEventDestroy(e);
+        for (auto& h : ctx->hs) {
+            if (h.buf) cudaFree(h.buf);
+            if (h.landed) cudaEventDestroy(h.landed);
+            if (h.done) cudaEventDestroy(h.done);
+        }
+        if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
         if (ctx->pf_side) cudaStreamDestroy(ctx->pf_side);
     }
     delete ctx;
@@ -940,6 +946,93 @@ dz_status dz_gdn_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_i
     if ((st = gdn_decode_impl(ctx, layer, B, seq_ids, dx, da, db, dzz, dy, s)) != DZ_OK) return st;
     DZ_CUDA(cudaMemcpyAsync(y, dy, ny * 4, cudaMemcpyDeviceToHost, s));
     DZ_CUDA(cudaStreamSynchronize(s));
+    return DZ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// overlapped host-buffer decode
+// ---------------------------------------------------------------------------
+// The inputs go up on the context's copy stream into a staging buffer of the
+// entry point's own; the caller's stream waits for them, runs the layer and
+// copies the output down.  The copy stream first waits for the previous call of
+// the same entry point to have finished with the buffer.  Nothing is
+// synchronised: the caller synchronises `stream` before reading the output or
+// reusing the input buffers.
+static dz_status host_stage(dz_ctx* ctx, int which, size_t bytes, cudaStream_t s, float** buf) {
+    dz_ctx::HostStage& h = ctx->hs[which];
+    if (!ctx->h2d) DZ_CUDA(cudaStreamCreateWithFlags(&ctx->h2d, cudaStreamNonBlocking));
+    if (!h.landed) DZ_CUDA(cudaEventCreateWithFlags(&h.landed, cudaEventDisableTiming));
+    if (!h.done) DZ_CUDA(cudaEventCreateWithFlags(&h.done, cudaEventDisableTiming));
+    if (h.bytes < bytes) {
+        if (h.buf) {
+            DZ_CUDA(cudaStreamSynchronize(s));           // the previous user of the buffer
+            cudaFree(h.buf);
+        }
+        h.buf = nullptr;
+        h.bytes = 0;
+        cudaError_t e = cudaMalloc(&h.buf, bytes);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, DZ_ENOMEM, "staging cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+        }
+        h.bytes = bytes;
+    }
+    DZ_CUDA(cudaStreamWaitEvent(ctx->h2d, h.done, 0));   // no-op before the first record
+    *buf = static_cast<float*>(h.buf);
+    return DZ_OK;
+}
+
+dz_status dz_gqa_decode_host_async(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* q_gate,
+                                   const float* k, const float* v, float* out, void* stream) {
+    dz_status st = gqa_decode_check(ctx, layer, B, seq_ids);
+    if (st != DZ_OK) return st;
+    if (!q_gate || !k || !v || !out) return fail(ctx, DZ_EINVAL, "null tensor");
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    const int kvc = ctx->cfg.kv_head_count, nq = GRP * kvc;
+    const size_t nqg = (size_t)B * nq * QG_ROW, nk = (size_t)B * kvc * HD, no = (size_t)B * nq * HD;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* dq = nullptr;
+    if ((st = host_stage(ctx, 0, (nqg + 2 * nk + no) * 4, s, &dq)) != DZ_OK) return st;
+    float* dk = dq + nqg;
+    float* dv = dk + nk;
+    float* dout = dv + nk;
+    DZ_CUDA(cudaMemcpyAsync(dq, q_gate, nqg * 4, cudaMemcpyHostToDevice, ctx->h2d));
+    DZ_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, ctx->h2d));
+    DZ_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, ctx->h2d));
+    DZ_CUDA(cudaEventRecord(ctx->hs[0].landed, ctx->h2d));
+    DZ_CUDA(cudaStreamWaitEvent(s, ctx->hs[0].landed, 0));
+    if ((st = gqa_decode_impl(ctx, layer, B, seq_ids, nullptr, dq, dk, dv, dout, s)) != DZ_OK) return st;
+    DZ_CUDA(cudaMemcpyAsync(out, dout, no * 4, cudaMemcpyDeviceToHost, s));
+    DZ_CUDA(cudaEventRecord(ctx->hs[0].done, s));
+    return DZ_OK;
+}
+
+dz_status dz_gdn_decode_host_async(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* qkv,
+                                   const float* alpha, const float* beta, const float* z, float* y, void* stream) {
+    dz_status st = gdn_decode_check(ctx, layer, B, seq_ids);
+    if (st != DZ_OK) return st;
+    if (!qkv || !alpha || !beta || !z || !y) return fail(ctx, DZ_EINVAL, "null tensor");
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(ctx, DZ_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+    const int vc = ctx->cfg.v_head_count;
+    const size_t nx = (size_t)B * QKV_LEN, na = (size_t)B * SSM_HV, nz = (size_t)B * INNER, ny = (size_t)B * vc * SSM_D;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* dx = nullptr;
+    if ((st = host_stage(ctx, 1, (nx + 2 * na + nz + ny) * 4, s, &dx)) != DZ_OK) return st;
+    float* da = dx + nx;
+    float* db = da + na;
+    float* dzz = db + na;
+    float* dy = dzz + nz;
+    DZ_CUDA(cudaMemcpyAsync(dx, qkv, nx * 4, cudaMemcpyHostToDevice, ctx->h2d));
+    DZ_CUDA(cudaMemcpyAsync(da, alpha, na * 4, cudaMemcpyHostToDevice, ctx->h2d));
+    DZ_CUDA(cudaMemcpyAsync(db, beta, na * 4, cudaMemcpyHostToDevice, ctx->h2d));
+    DZ_CUDA(cudaMemcpyAsync(dzz, z, nz * 4, cudaMemcpyHostToDevice, ctx->h2d));
+    DZ_CUDA(cudaEventRecord(ctx->hs[1].landed, ctx->h2d));
+    DZ_CUDA(cudaStreamWaitEvent(s, ctx->hs[1].landed, 0));
+    if ((st = gdn_decode_impl(ctx, layer, B, seq_ids, dx, da, db, dzz, dy, s)) != DZ_OK) return st;
+    DZ_CUDA(cudaMemcpyAsync(y, dy, ny * 4, cudaMemcpyDeviceToHost, s));
+    DZ_CUDA(cudaEventRecord(ctx->hs[1].done, s));
     return DZ_OK;
 }
 

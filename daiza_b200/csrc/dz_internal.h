@@ -108,6 +108,14 @@ struct dz_ctx {
     // Gated DeltaNet prefill: side stream of the intra-chunk kernels and the events
     // that order them with the chain kernels (created with the context)
     cudaStream_t pf_side = nullptr;
+    // overlapped host-buffer decode (dz_*_decode_host_async): a copy stream, and per
+    // entry point a staging buffer with "inputs landed" / "buffer free" events
+    cudaStream_t h2d = nullptr;
+    struct HostStage {
+        void* buf = nullptr;
+        size_t bytes = 0;
+        cudaEvent_t landed = nullptr, done = nullptr;
+    } hs[2];                     // 0: gated GQA, 1: Gated DeltaNet
     cudaEvent_t pf_ev[dz::PF_MAX_SEGMENTS + 1] = {};
     // sequence snapshots: slots of snap_slot_floats floats each (sized by the config)
     float* snap_mem = nullptr;

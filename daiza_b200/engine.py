@@ -283,22 +283,27 @@ class Context:
                                           _ptr(y), _stream(stream)))
 
     # ---- compute (host arrays; end-to-end path) ----------------------------
-    def gqa_decode_host(self, layer, seq_ids, q_gate, k, v, out=None, stream=None):
+    def gqa_decode_host(self, layer, seq_ids, q_gate, k, v, out=None, stream=None, sync=True):
+        """sync=False: dz_gqa_decode_host_async -- the caller synchronises `stream`
+        before reading `out` or reusing the inputs."""
         ids = np.ascontiguousarray(np.atleast_1d(seq_ids), np.int32)
         B = len(ids)
         if out is None:
             out = np.empty((B, self.nq * HD), np.float32)
-        self._chk(self.lib.dz_gqa_decode_host(self.h, layer, B, _np_ptr(ids), _np_ptr(q_gate), _np_ptr(k),
-                                              _np_ptr(v), _np_ptr(out), _stream(stream)))
+        fn = self.lib.dz_gqa_decode_host if sync else self.lib.dz_gqa_decode_host_async
+        self._chk(fn(self.h, layer, B, _np_ptr(ids), _np_ptr(q_gate), _np_ptr(k), _np_ptr(v), _np_ptr(out),
+                     _stream(stream)))
         return out
 
-    def gdn_decode_host(self, layer, seq_ids, qkv, alpha, beta, z, y=None, stream=None):
+    def gdn_decode_host(self, layer, seq_ids, qkv, alpha, beta, z, y=None, stream=None, sync=True):
+        """sync=False: dz_gdn_decode_host_async (see gqa_decode_host)."""
         ids = np.ascontiguousarray(np.atleast_1d(seq_ids), np.int32)
         B = len(ids)
         if y is None:
             y = np.empty((B, self.vc * SSM_D), np.float32)
-        self._chk(self.lib.dz_gdn_decode_host(self.h, layer, B, _np_ptr(ids), _np_ptr(qkv), _np_ptr(alpha),
-                                              _np_ptr(beta), _np_ptr(z), _np_ptr(y), _stream(stream)))
+        fn = self.lib.dz_gdn_decode_host if sync else self.lib.dz_gdn_decode_host_async
+        self._chk(fn(self.h, layer, B, _np_ptr(ids), _np_ptr(qkv), _np_ptr(alpha), _np_ptr(beta), _np_ptr(z),
+                     _np_ptr(y), _stream(stream)))
         return y
 
 

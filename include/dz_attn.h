@@ -279,6 +279,18 @@ dz_status dz_gqa_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_i
 dz_status dz_gdn_decode_host(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* qkv,
                              const float* alpha, const float* beta, const float* z, float* y, void* stream);
 
+/* The same two calls without the final synchronisation, for overlapping one
+ * call's input upload with the previous call's work: the inputs go up on a
+ * context-owned copy stream into a staging buffer per entry point (the upload
+ * waits until the previous call of the same entry point has finished with
+ * it), `stream` waits for them, runs the layer and queues the output download.
+ * The caller synchronises `stream` before reading `out`/`y` or reusing the
+ * input buffers; host buffers should be pinned for the copies to overlap. */
+dz_status dz_gqa_decode_host_async(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* q_gate,
+                                   const float* k, const float* v, float* out, void* stream);
+dz_status dz_gdn_decode_host_async(dz_ctx* ctx, int layer, int B, const int32_t* seq_ids, const float* qkv,
+                                   const float* alpha, const float* beta, const float* z, float* y, void* stream);
+
 /* dz_gqa_decode without any device allocation, for callers that cannot call
  * cudaMalloc: engines whose device memory is owned end to end by their own
  * allocator, and decode loops that must not risk the implicit device

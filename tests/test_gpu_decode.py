@@ -204,6 +204,45 @@ def test_host_entry_points_match_device(dz):
     ctx.close()
 
 
+def test_async_host_entry_points_match_sync(dz):
+    """dz_*_decode_host_async: three steps of GQA + DeltaNet on 3 sequences
+    with one stream synchronisation per step (uploads of one call overlapping
+    the previous call's kernels) give the same bytes as the synchronous calls
+    on a twin context."""
+    seed = O.SEED0 + 73
+    B = 3
+    ids = np.arange(B, dtype=np.int32)
+    ctxs = []
+    for _ in range(2):
+        ctx, _, _ = make_ctx(dz, [800] * B, seed=seed)
+        for s in range(B):
+            _, _, _, kf, vf = O.gqa_decode_inputs(seed + 10 * s, 300 + 50 * s)
+            ctx.kv_import(1, s, kf, vf)
+            _, _, _, _, hist, state = O.gdn_decode_inputs(seed + 10 * s)
+            ctx.ssm_import(0, s, state, hist, s % 4)
+        ctxs.append(ctx)
+    sync_ctx, async_ctx = ctxs
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
+    for step in range(3):
+        sd = seed + 1000 + step
+        qg, k, v = O.normal(sd, (B, 12288)), O.normal(sd + 1, (B, 1024)), O.normal(sd + 2, (B, 1024))
+        qkv, a, b, z = (O.normal(sd + 3, (B, 10240)), O.normal(sd + 4, (B, 48)), O.normal(sd + 5, (B, 48)),
+                        O.normal(sd + 6, (B, 6144)))
+        want_o = sync_ctx.gqa_decode_host(1, ids, qg, k, v)
+        want_y = sync_ctx.gdn_decode_host(0, ids, qkv, a, b, z)
+        ins = [pin(x) for x in (qg, k, v, qkv, a, b, z)]
+        out_o = pin(np.zeros((B, 6144), np.float32))
+        out_y = pin(np.zeros((B, 6144), np.float32))
+        async_ctx.gqa_decode_host(1, ids, ins[0], ins[1], ins[2], out_o, sync=False)
+        async_ctx.gdn_decode_host(0, ids, ins[3], ins[4], ins[5], ins[6], out_y, sync=False)
+        torch.cuda.synchronize()
+        assert np.array_equal(out_o, want_o), f"GQA step {step}"
+        assert np.array_equal(out_y, want_y), f"DeltaNet step {step}"
+    for c in ctxs:
+        assert c.device_error() == 0
+        c.close()
+
+
 def test_error_paths(dz):
     from daiza_b200 import DzError
     ctx, _, _ = make_ctx(dz, [2])
