@@ -126,7 +126,7 @@ struct dz_ctx {
 namespace dz {
 // Positions per split-K work item of a GQA decode launch (shared by every decode
 // entry point so they split a batch the same way): ~4 items per resident warp
-// (4 warps per SM) over the whole batch, 16..1024 positions, at most MAXC chunks
+// of the original 4-warp split kernel (2 per warp of the current 8) over the whole batch, 16..1024 positions, at most MAXC chunks
 // per (sequence, kv head), a multiple of 16.  total / nmax: sum and max of
 // len + 1 over the batch.
 #ifndef DZ_DECODE_CHUNK_MIN

@@ -8,9 +8,9 @@
 //                     slot len.
 //   2. gqa_split    : per (sequence, split-K chunk, kv head), one warp each --
 //                     the 6 grouped q heads attend over the chunk's cached
-//                     positions.  K/V tiles of 8 positions stream HBM -> shared
+//                     positions.  K/V tiles of 4 positions stream HBM -> shared
 //                     memory through 1-D bulk async copies (cp.async.bulk +
-//                     mbarrier, 3 stages per warp); scores on the FP32 pipes
+//                     mbarrier, 2 stages per warp, 8 warps per SM); scores on the FP32 pipes
 //                     with a warp-shuffle reduce-scatter, online softmax in
 //                     log2 units, unnormalised partials out.  A programmatic
 //                     dependent of 1: old K/V tiles stream in while 1 finishes.
@@ -25,7 +25,7 @@
 
 namespace dz {
 
-constexpr int STAGES = 3;
+constexpr int STAGES = 2;
 
 // ---------------------------------------------------------------------------
 // Per-head prologue (attention.rs:92-113) on a loaded head row: RMSNorm
@@ -109,20 +109,23 @@ __global__ void __launch_bounds__(256) gqa_prep_kernel(GqaDecodeDesc d, int kvc,
 
 // ---------------------------------------------------------------------------
 // 2. split-K attention, one WARP per work item (sequence, chunk, kv head).
-//    Persistent CTAs of 4 independent warps (one CTA per SM).  Each warp walks
-//    its own items and keeps its own ring of STAGES tiles of 8 positions in
-//    shared memory, refilled by its lane 0 with two 1-D bulk async copies per
-//    tile (K rows and V rows are each one contiguous run), across item
-//    boundaries.  No CTA-wide barrier after set-up.
+//    Persistent CTAs of 8 independent warps (one CTA per SM, two warps per
+//    sub-partition so one warp's stalls hide under the other's work).  Each
+//    warp walks its own items and keeps its own ring of STAGES tiles of 4
+//    positions in shared memory, refilled by its lane 0 with two 1-D bulk async
+//    copies per tile (K rows and V rows are each one contiguous run), across
+//    item boundaries.  No CTA-wide barrier after set-up.  (Measured on config 2:
+//    8 warps x 2 stages x 4 positions 0.93 of HBM; 4 warps x 3 x 8 positions
+//    0.85; 12 warps exceed the register file.)
 //    Lane l owns dims [4l,4l+4) and [128+4l,128+4l+4) of q (6 heads, in
 //    registers), K, V and the output accumulators.
-//    QK: 48 partial dot products per lane (8 positions x 6 heads), combined by
-//        a 5-level reduce-scatter (48 shuffles per tile).
+//    QK: 24 partial dot products per lane (4 positions x 6 heads), combined by
+//        a reduce-scatter over lane bits 16, 8, 4 and sums over bits 2, 1.
 //    softmax: lanes 0..5 own heads (running max in log2 units, sum).
 //    PV: every lane accumulates its 8 dims x 6 heads.
 // ---------------------------------------------------------------------------
-constexpr int TP = 8;        // positions per tile
-constexpr int NWARP = 4;     // warps per CTA
+constexpr int TP = 4;        // positions per tile
+constexpr int NWARP = 8;     // warps per CTA
 
 // alignas(128): every warp's ring (and its K/V tiles, the bulk-copy
 // destinations) must start on a 16-byte boundary, so the struct size must be a
@@ -181,7 +184,7 @@ __device__ __forceinline__ void rs_level(const float (&in)[2 * N], float (&out)[
     }
 }
 
-__global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaDecodeDesc d, int kvc, const KvSlot* __restrict__ kv,
+__global__ void __launch_bounds__(32 * NWARP, 1) gqa_split_kernel(GqaDecodeDesc d, int kvc, const KvSlot* __restrict__ kv,
                                                            const float* __restrict__ q_buf,
                                                            float* __restrict__ part_o,
                                                            float* __restrict__ part_ml, int* err, int n_items) {
@@ -231,10 +234,10 @@ __global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaDecodeDesc d, int 
     for (int s = 0; s < STAGES; ++s) produce(s);
     wait_prep();   // q_buf comes from gqa_prep
 
-    const int k_grp = lane >> 1;              // reduce-scatter group: indices 3k..3k+2 of (pos*6 + head)
+    const int k_grp = lane >> 2;              // reduce-scatter group: indices 3k..3k+2 of (pos*6 + head)
     const int my_pos = k_grp >> 1;
     const int my_h0 = 3 * (k_grp & 1);
-    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
     int j = 0;
     for (int item = gw; item < n_items; item += nw) {
         const ItemInfo it = decode_item(d, kvc, kv, item);
@@ -277,15 +280,17 @@ __global__ void __launch_bounds__(128, 1) gqa_split_kernel(GqaDecodeDesc d, int 
                     part[p * GRP + h] = a;
                 }
             }
-            // ---- reduce-scatter 48 -> 3 per lane pair (indices 3*k_grp .. 3*k_grp+2)
-            float r24[24], r12[12], r6[6], r3[3];
-            rs_level<24>(part, r24, b4, 16);
-            rs_level<12>(r24, r12, b3, 8);
-            rs_level<6>(r12, r6, b2, 4);
-            rs_level<3>(r6, r3, b1, 2);
+            // ---- reduce-scatter 24 -> 3 per lane quad (indices 3*k_grp .. 3*k_grp+2)
+            float r12[12], r6[6], r3[3];
+            rs_level<12>(part, r12, b4, 16);
+            rs_level<6>(r12, r6, b3, 8);
+            rs_level<3>(r6, r3, b2, 4);
 #pragma unroll
-            for (int i = 0; i < 3; ++i) r3[i] += __shfl_xor_sync(0xffffffffu, r3[i], 1);
-            if ((lane & 1) == 0) {
+            for (int i = 0; i < 3; ++i) {
+                r3[i] += __shfl_xor_sync(0xffffffffu, r3[i], 2);
+                r3[i] += __shfl_xor_sync(0xffffffffu, r3[i], 1);
+            }
+            if ((lane & 3) == 0) {
 #pragma unroll
                 for (int i = 0; i < 3; ++i) R.sc[my_pos][my_h0 + i] = r3[i] * LOG2E;
             }
