@@ -55,8 +55,10 @@ __global__ void __launch_bounds__(256) gdn_dec_prep_kernel(GdnDecodeDesc d, int 
                                                            const float* __restrict__ beta_in,
                                                            const float* __restrict__ z_in, float* __restrict__ qk,
                                                            float* __restrict__ rec) {
-    // the state kernel may start its tile copies now; it waits for this grid's
-    // writes before reading q/k/records
+    // a programmatic dependent of whatever precedes it: wait for that grid (the
+    // states and rings may still be in use by it), then let the state kernel start
+    // its tile copies; it waits for this grid's writes before reading q/k/records
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     const int b = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -316,7 +318,10 @@ __global__ void __launch_bounds__(32 * (SSM_D / RS / 8)) gdn_dec_kernel(
     constexpr int ROWS = Smem::ROWS;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
-    // a programmatic successor (the next projection) may start streaming its weights
+    // launched as a programmatic dependent of whatever precedes it: wait for that
+    // grid (the state may still be in use by it) before anything else; then a
+    // programmatic successor (the next projection) may start streaming its weights
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int item = blockIdx.x / RS;                 // b * vc + vl
@@ -471,8 +476,20 @@ static cudaError_t launch_two_pass(dz_ctx* ctx, int layer, const GdnDecodeDesc& 
     float* qk = ctx->gdn_rec;
     float* rec = qk + qk_floats;
     const int n_chunks = (2 * SSM_HK + vc + PREP_GROUPS - 1) / PREP_GROUPS;
-    gdn_dec_prep_kernel<<<dim3(d.B, n_chunks + 1), 256, 0, st>>>(d, vh0, vc, L.d_ssm, L.conv_w, L.ssm_a, L.dt_bias,
-                                                                qkv, alpha, beta, z, qk, rec);
+    {
+        cudaLaunchAttribute ap[1];
+        ap[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        ap[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t lp{};
+        lp.gridDim = dim3(d.B, n_chunks + 1);
+        lp.blockDim = dim3(256);
+        lp.stream = st;
+        lp.attrs = ap;
+        lp.numAttrs = 1;
+        e = cudaLaunchKernelEx(&lp, gdn_dec_prep_kernel, d, vh0, vc, (const SsmSlot*)L.d_ssm, (const float*)L.conv_w,
+                               (const float*)L.ssm_a, (const float*)L.dt_bias, qkv, alpha, beta, z, qk, rec);
+        if (e != cudaSuccess) return e;
+    }
     e = cudaFuncSetAttribute(gdn_dec_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(GdnSmem));
     if (e != cudaSuccess) return e;
     // programmatic dependent launch: the state kernel's CTAs start their first
@@ -507,13 +524,15 @@ static cudaError_t launch_rs(dz_ctx* ctx, const LayerState& L, const GdnDecodeDe
     lc.blockDim = dim3(32 * (SSM_D / RS / 8));
     lc.dynamicSmemBytes = smem;
     lc.stream = st;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = RS;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     lc.attrs = at;
-    lc.numAttrs = 1;
+    lc.numAttrs = 2;
     return cudaLaunchKernelEx(&lc, kern, d, vh0, vc, (const SsmSlot*)L.d_ssm, (const float*)L.conv_w,
                               (const float*)L.ssm_a, (const float*)L.dt_bias, (const float*)L.norm_w, qkv, alpha,
                               beta, z, y, ctx->d_err);

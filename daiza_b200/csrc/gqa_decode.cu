@@ -69,8 +69,11 @@ __global__ void __launch_bounds__(256) gqa_prep_kernel(GqaDecodeDesc d, int kvc,
                                                        const float* __restrict__ k_in,
                                                        const float* __restrict__ v_in,
                                                        float* __restrict__ q_buf, float eps) {
-    // the split grid may launch now: it streams old K/V tiles and waits for this
-    // grid before it reads q_buf or the appended row
+    // Launched as a programmatic dependent of whatever precedes it: wait for that
+    // grid first (inputs, q_buf and the caches may still be in use by it), and only
+    // then let the split grid launch -- the split grid streams old K/V tiles before
+    // its own wait, so every earlier append must be complete by then.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     const int b = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -432,9 +435,10 @@ __global__ void __launch_bounds__(32 * CMB_MAX_GROUPS) gqa_combine_kernel(GqaDec
     }
 }
 
-// prep (plain launch: it follows whatever came before in the stream), then the
-// split grid as a programmatic dependent of prep (old K/V tiles stream in while
-// prep finishes) and the combine grid as a programmatic dependent of split.
+// prep as a programmatic dependent of whatever came before in the stream (it
+// waits for that grid before anything else), then the split grid as a
+// programmatic dependent of prep (old K/V tiles stream in while prep finishes)
+// and the combine grid as a programmatic dependent of split.
 cudaError_t launch_gqa_decode_scratch(dz_ctx* ctx, int layer, const GqaDecodeDesc& d, const float* q_gate,
                                       const float* k, const float* v, float* out, cudaStream_t st, int* n_launch,
                                       float* q_buf, float* part_o, float* part_ml) {
@@ -446,12 +450,21 @@ cudaError_t launch_gqa_decode_scratch(dz_ctx* ctx, int layer, const GqaDecodeDes
     cudaError_t e = cudaFuncSetAttribute(gqa_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sizeof(SplitSmem));
     if (e != cudaSuccess) return e;
-    gqa_prep_kernel<<<dim3(d.B, (GRP * kvc + kvc + 7) / 8), 256, 0, st>>>(d, kvc, L.d_kv, L.q_norm, L.k_norm,
-                                                                          ctx->rope, q_gate, k, v, q_buf,
-                                                                          ctx->cfg.rms_eps);
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = 1;
+    {
+        cudaLaunchConfig_t lp{};
+        lp.gridDim = dim3(d.B, (GRP * kvc + kvc + 7) / 8);
+        lp.blockDim = dim3(256);
+        lp.stream = st;
+        lp.attrs = at;
+        lp.numAttrs = 1;
+        e = cudaLaunchKernelEx(&lp, gqa_prep_kernel, d, kvc, (const KvSlot*)L.d_kv, (const float*)L.q_norm,
+                               (const float*)L.k_norm, (const float*)ctx->rope, q_gate, k, v, q_buf,
+                               ctx->cfg.rms_eps);
+        if (e != cudaSuccess) return e;
+    }
     cudaLaunchConfig_t lc{};
     lc.gridDim = dim3(std::min((items + NWARP - 1) / NWARP, ctx->n_sm));
     lc.blockDim = dim3(32 * NWARP);
