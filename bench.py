@@ -52,10 +52,10 @@ SSM_HV, SSM_D, QKV_LEN, INNER = 48, 128, 10240, 6144
 
 # DRAM bytes (read + write) that one ncu capture counted for the split-K
 # attention kernel, divided by the algorithmic bytes of that launch: the first
-# 16 config-2 sequences (205,050 KV positions, 1.681 GB algorithmic, 1.696 GB
+# 16 config-2 sequences (205,050 KV positions, 1.681 GB algorithmic, 1.692 GB
 # counted).  Traffic grows with the KV positions read, so the roofline's
 # `traffic` is this ratio times the algorithmic bytes of the timed launch.
-GQA_SPLIT_TRAFFIC_RATIO = 1.0087
+GQA_SPLIT_TRAFFIC_RATIO = 1.0066
 
 
 def seq_lengths():
