@@ -34,11 +34,12 @@
 //      CTAs is summed in a fixed order by the CTA that finishes it last
 //      (partials in scratch, a counter per block that the reducing CTA
 //      resets), so results do not depend on timing.
-// Why mma.sync: a tcgen05.mma with M = 128 occupies the tensor core for about
-// 200 cycles at any N from 16 to 256, so with N = 3T <= 24 it would process
-// 128 x 32 weights per 200 cycles -- a tenth of the HBM rate.  The register-
-// operand m16n8k32 runs at about 0.4 per cycle per SM (512 weights each) and
-// needs no shared-memory staging of the expanded signs.
+// Why mma.sync: a tcgen05.mma kind::i8 with M = 128 and K = 32 takes about 58
+// cycles per SM at any N up to 64 (143 at N = 256), so with N = 3T <= 24 it
+// processes 128 x 32 weights per ~58 cycles -- about 70 weights per cycle per
+// SM, under half of the HBM rate.  The register-operand m16n8k32 runs at about
+// 0.4 per cycle per SM (512 weights each, ~200 weights per cycle) and needs no
+// staging of the expanded signs in shared or tensor memory.
 // The only rounding beyond f32 accumulation is the input quantisation (~1e-7 of
 // the group's max|x| per element).  Roofline: HBM -- the Q1_0 bytes (1.125 bits
 // per weight) are read once.
