@@ -1,5 +1,5 @@
-// q1_gemv.cu -- Q1_0 projection GEMV for a few tokens on the tcgen05 integer
-// tensor cores.
+// q1_gemv.cu -- Q1_0 projection GEMV for a few tokens on the integer tensor
+// cores (warp-level mma.sync, see "Why mma.sync" below).
 //
 // Reference: Daiza-engine/src/model/weights.rs:831 (matvec_multi_into_slice: up
 // to 8 Q1_0 matrices sharing one input row), weights.rs:334
@@ -18,9 +18,9 @@
 //      columns zero); prep writes the B fragments of mma.m16n8k32 in register
 //      order, per group and K step, plus per column the factor 2 * 256^p * s_tg
 //      and (plane 0 only) the term s_tg * sum q.
-//   2. q1_gemv (persistent, a programmatic dependent of 1): the work is a list
-//      of items (128-row block, 8 groups), cut into equal contiguous ranges,
-//      one per CTA.  A loader thread brings each item's 128 x 144 weight bytes
+//   2. q1_gemv (a programmatic dependent of 1): the work is a list of items
+//      (128-row block, 8 groups); each cluster takes a contiguous range of row
+//      blocks and each CTA of it a range of every block's items.  A loader thread brings each item's 128 x 144 weight bytes
 //      (one 2-D TMA box of the Q1_0 rows) and its 8 groups of B fragments into
 //      a two-slot ring.  Warp w of 8 takes rows 16w .. 16w+15: per group, lane
 //      (g, q) reads sign word q of rows g and g+8 and turns it into A fragments
@@ -30,10 +30,11 @@
 //      sums the set bits' digits exactly over the group; each int32 column
 //      value then enters an f32 sum per (row, column) as
 //      scale * (factor * a - term).  When a block is complete the 3 plane
-//      columns of each token are added into y.  A row block split between
-//      CTAs is summed in a fixed order by the CTA that finishes it last
-//      (partials in scratch, a counter per block that the reducing CTA
-//      resets), so results do not depend on timing.
+//      columns of each token are added into y.  When there are fewer row
+//      blocks than CTA slots, a block's units are split over a cluster of 2 or
+//      4 CTAs; each stores its row sums into rank 0's shared memory (distributed
+//      shared memory) and rank 0 adds them in rank order, so results do not
+//      depend on timing.
 // Why mma.sync: a tcgen05.mma kind::i8 with M = 128 and K = 32 takes about 58
 // cycles per SM at any N up to 64 (143 at N = 256), so with N = 3T <= 24 it
 // processes 128 x 32 weights per ~58 cycles -- about 70 weights per cycle per
