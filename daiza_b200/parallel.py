@@ -179,15 +179,18 @@ class ShardedStack:
         self.n_seqs = n_seqs
         self._bufs = {}
 
-    def _gather(self, t):
-        """all_gather_rows into a buffer kept per (shape, dtype)."""
+    def _gather(self, t, kind):
+        """all_gather_rows into a buffer kept per (layer kind, shape, dtype): the
+        GQA and DeltaNet outputs can have the same shape (2 ranks: 12 q heads x 256
+        = 24 v heads x 128), and each kind's last gathered result must survive the
+        other kind's gathers."""
         import torch
         if self.world == 1:
             return [t]
-        key = (tuple(t.shape), t.dtype)
+        key = (kind, tuple(t.shape), t.dtype)
         buf = self._bufs.get(key)
         if buf is None:
-            buf = self._bufs[key] = torch.empty((self.world,) + key[0], dtype=t.dtype, device=t.device)
+            buf = self._bufs[key] = torch.empty((self.world,) + key[1], dtype=t.dtype, device=t.device)
         return all_gather_rows(t, self.group, out=buf)
 
     # inputs: dict with full-width tensors; slices are taken once by the caller
@@ -216,10 +219,10 @@ class ShardedStack:
         for layer in range(self.n_layers):
             if self.attn[layer]:
                 self.ctx.gqa_decode(layer, rows, qg, ks, vs, out)
-                last["gqa"] = self._gather(out)
+                last["gqa"] = self._gather(out, "gqa")
             else:
                 self.ctx.gdn_decode(layer, all_rows, *gdn_in, y)
-                last["gdn"] = self._gather(y)
+                last["gdn"] = self._gather(y, "gdn")
         return (assemble_gqa(last["gqa"], self.plans, self.n_seqs) if "gqa" in last else None,
                 assemble_gdn(last["gdn"], self.plans) if "gdn" in last else None)
 
@@ -236,10 +239,10 @@ class ShardedStack:
         for layer in range(self.n_layers):
             if self.attn[layer]:
                 self.ctx.gqa_prefill(layer, seq, qg, ks, vs, out)
-                last["gqa"] = self._gather(out)
+                last["gqa"] = self._gather(out, "gqa")
             else:
                 self.ctx.gdn_prefill(layer, seq, *gdn_in, y)
-                last["gdn"] = self._gather(y)
+                last["gdn"] = self._gather(y, "gdn")
         return (assemble_gqa_prefill(last["gqa"], self.plans) if "gqa" in last else None,
                 assemble_gdn(last["gdn"], self.plans) if "gdn" in last else None)
 

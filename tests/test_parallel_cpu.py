@@ -70,3 +70,26 @@ def test_gather_assembly_two_ranks_gloo():
     for p in procs:
         p.join(timeout=60)
     assert all(ok1 and ok2 for _, ok1, ok2 in res), res
+
+
+def test_gather_buffers_are_kept_per_layer_kind(monkeypatch):
+    """With 2 ranks the GQA output of a layer ([rows, 12 x 256]) and the
+    DeltaNet output ([rows, 24 x 128]) have the same shape; the per-shape
+    gather buffer must not be shared between the two kinds, or the DeltaNet
+    result returned by decode_step/prefill would be overwritten by the GQA
+    layer gathered after it."""
+    import torch
+    from daiza_b200 import parallel as P
+
+    def fake_gather(local, group=None, out=None):
+        for r in range(out.shape[0]):
+            out[r].copy_(local + r)
+        return list(out.unbind(0))
+
+    monkeypatch.setattr(P, "all_gather_rows", fake_gather)
+    st = P.ShardedStack.__new__(P.ShardedStack)
+    st.world, st.group, st._bufs = 2, None, {}
+    gdn = st._gather(torch.zeros(4, 3072), "gdn")
+    gqa = st._gather(torch.full((4, 3072), 100.0), "gqa")
+    assert float(gdn[0].max()) == 0.0 and float(gdn[1].max()) == 1.0
+    assert float(gqa[0].min()) == 100.0
