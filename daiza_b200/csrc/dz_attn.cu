@@ -790,13 +790,9 @@ static dz_status gqa_decode_impl(dz_ctx* ctx, int layer, int B, const int32_t* s
         const int nb = std::min(MAXB, B - b0);
         GqaDecodeDesc d;
         d.B = nb;
-        int64_t total = 0, nmax = 0;
-        for (int b = 0; b < nb; ++b) {
-            const int64_t n = L.len[seq_ids[b0 + b]] + 1;
-            total += n;
-            nmax = std::max(nmax, n);
-        }
-        const int64_t chunk = decode_chunk(ctx->n_sm, kvc, total, nmax);
+        int64_t nlen[MAXB];
+        for (int b = 0; b < nb; ++b) nlen[b] = L.len[seq_ids[b0 + b]] + 1;
+        const int64_t chunk = decode_chunk_balanced(ctx->n_sm, kvc, nlen, nb, ctx->part_items);
         d.chunk = (int)chunk;
         d.cum[0] = 0;
         for (int b = 0; b < nb; ++b) {

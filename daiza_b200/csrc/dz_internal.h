@@ -1,5 +1,6 @@
 // dz_internal.h -- host-side context and launcher declarations for libdzattn.
 #pragma once
+#include <algorithm>
 #include <string>
 #include <vector>
 #include <cuda_runtime.h>
@@ -138,6 +139,64 @@ inline int64_t decode_chunk(int n_sm, int kvc, int64_t total, int64_t nmax) {
     const int64_t need = (nmax + MAXC - 1) / MAXC;
     if (chunk < need) chunk = need;
     return (chunk + 15) / 16 * 16;
+}
+
+// Warps of the split-K attention kernel per CTA (one CTA per SM, one work item
+// per warp at a time, items handed out round-robin: item i -> warp i % W).
+constexpr int GQA_SPLIT_WARPS = 8;
+
+// The chunk actually used by dz_gqa_decode: decode_chunk and a few chunks that
+// give about k items per warp (k = 1..8), each scored by the largest sum of
+// positions (plus a per-item cost of 16 positions) that one warp gets under the
+// kernel's round-robin hand-out; the smallest score wins, ties to the larger
+// chunk.  Candidates with more than max_items items are skipped (decode_chunk
+// itself always fits the scratch bound below).  n[b] = len + 1.
+inline int64_t decode_chunk_balanced(int n_sm, int kvc, const int64_t* n, int B, int64_t max_items) {
+    int64_t total = 0, nmax = 0;
+    for (int b = 0; b < B; ++b) {
+        total += n[b];
+        nmax = n[b] > nmax ? n[b] : nmax;
+    }
+    const int64_t base = decode_chunk(n_sm, kvc, total, nmax);
+    int64_t cmin = (nmax + MAXC - 1) / MAXC;
+    cmin = cmin < 16 ? 16 : (cmin + 15) / 16 * 16;
+    const int64_t W_full = (int64_t)n_sm * GQA_SPLIT_WARPS;
+    std::vector<int64_t> load((size_t)W_full);
+    auto score = [&](int64_t c) -> int64_t {
+        int64_t items = 0;
+        for (int b = 0; b < B; ++b) items += (n[b] + c - 1) / c;
+        items *= kvc;
+        if (items > max_items) return -1;
+        int64_t ctas = (items + GQA_SPLIT_WARPS - 1) / GQA_SPLIT_WARPS;
+        if (ctas > n_sm) ctas = n_sm;
+        const int64_t W = ctas * GQA_SPLIT_WARPS;
+        std::fill(load.begin(), load.begin() + W, 0);
+        int64_t idx = 0, worst = 0;
+        for (int b = 0; b < B; ++b)
+            for (int64_t p0 = 0; p0 < n[b]; p0 += c) {
+                const int64_t size = (n[b] - p0 < c ? n[b] - p0 : c) + 16;
+                for (int h = 0; h < kvc; ++h, ++idx) {
+                    int64_t& l = load[(size_t)(idx % W)];
+                    l += size;
+                    worst = l > worst ? l : worst;
+                }
+            }
+        return worst;
+    };
+    int64_t best = base, best_score = score(base);
+    for (int k = 1; k <= 8; ++k) {
+        int64_t c = (total * kvc + k * W_full - 1) / (k * W_full);
+        c = (c + 15) / 16 * 16;
+        c = c < cmin ? cmin : (c > 1024 ? 1024 : c);
+        if (c < cmin) continue;
+        const int64_t sc = score(c);
+        if (sc < 0) continue;
+        if (best_score < 0 || sc < best_score || (sc == best_score && c > best)) {
+            best = c;
+            best_score = sc;
+        }
+    }
+    return best;
 }
 
 // Upper bound on the split-K work items of one decode launch of at most B

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(256) gqa_prep_kernel(GqaDecodeDesc d, int kvc,
 //    PV: every lane accumulates its 8 dims x 6 heads.
 // ---------------------------------------------------------------------------
 constexpr int TP = 4;        // positions per tile
-constexpr int NWARP = 8;     // warps per CTA
+constexpr int NWARP = GQA_SPLIT_WARPS;     // warps per CTA (8)
 
 // alignas(128): every warp's ring (and its K/V tiles, the bulk-copy
 // destinations) must start on a 16-byte boundary, so the struct size must be a
