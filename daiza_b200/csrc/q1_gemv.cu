@@ -20,9 +20,9 @@
 //      and (plane 0 only) the term s_tg * sum q.
 //   2. q1_gemv (a programmatic dependent of 1): the work is a list of items
 //      (128-row block, 8 groups); each cluster takes a contiguous range of row
-//      blocks and each CTA of it a range of every block's items.  A loader thread brings each item's 128 x 144 weight bytes
-//      (one 2-D TMA box of the Q1_0 rows) and its 8 groups of B fragments into
-//      a two-slot ring.  Warp w of 8 takes rows 16w .. 16w+15: per group, lane
+//      blocks and each CTA of it a range of every block's items.  A loader
+//      thread brings each item's 128 x 144 weight bytes (one 2-D TMA box of
+//      the Q1_0 rows) and its 8 groups of B fragments into a two-slot ring.  Warp w of 8 takes rows 16w .. 16w+15: per group, lane
 //      (g, q) reads sign word q of rows g and g+8 and turns it into A fragments
 //      with (word >> s) & 0x01010101 -- bits s, s+8, s+16, s+24 as 0/1 bytes --
 //      so K step s of the group uses bits s and s+4 of every word, and the B
